@@ -1,0 +1,176 @@
+/*
+ * jishui_b200.h — C ABI of the B200 (sm_100a) kernels behind the Jishui
+ * decoder training step.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensors are device pointers owned by the caller (torch allocates
+ *     them). Sizes and leading dimensions are in elements.
+ *   - "f16" buffers hold IEEE binary16, "f32" buffers binary32.
+ *   - Each call is stream-ordered on `stream` (the caller's current CUDA
+ *     stream) and never synchronises the host.
+ *   - The return value is JX_OK (0) or a negative JX_ERR_* code; the text of
+ *     the most recent failure on the calling thread is returned by
+ *     jx_last_error().
+ *   - The library allocates no device memory on any call. Scratch space (the
+ *     split-K partials of the weight-gradient GEMM) is passed in by the
+ *     caller; jx_gemm_wgrad_workspace_bytes() gives its size.
+ *
+ * Reference interfaces replaced (paths are inside the Midstream-LLM project):
+ *   src/jishui/model_torch.py:12-15   nn.RMSNorm            -> jx_rmsnorm_fwd / jx_rmsnorm_bwd
+ *   src/jishui/model_torch.py:18-25   rope()                -> jx_gemm_qkv_rope epilogue, jx_attn_bwd rope_* args
+ *   src/jishui/model_torch.py:41-43   q/k/v nn.Linear       -> jx_gemm_qkv_rope, jx_gemm_f16, jx_gemm_wgrad
+ *   src/jishui/model_torch.py:48      F.scaled_dot_product_attention(is_causal=True) -> jx_attn_fwd / jx_attn_bwd
+ *   src/jishui/model_torch.py:49,72   o_proj + residual add -> jx_gemm_f16 (residual epilogue)
+ *   src/jishui/model_torch.py:59-60   SwiGLU                -> jx_gemm_swiglu_fwd / jx_gemm_swiglu_bwd
+ *   src/jishui/model_torch.py:89-93   nn.Embedding + cast   -> jx_embed_fwd / jx_embed_bwd
+ *   src/jishui/model_torch.py:98      tied head F.linear    -> jx_gemm_f16 (+ jx_gemm_wgrad for dE)
+ *   src/jishui/model_torch.py:102-104 F.cross_entropy(logits.float()) -> jx_ce_fwd / jx_ce_loss / jx_ce_bwd
+ *   src/jishui/pretrain_torch.py:218-219 GradScaler.unscale_ + clip_grad_norm_ -> jx_grad_stats / jx_grad_finalize
+ *   src/jishui/pretrain_torch.py:119-120,231 AdamW(fused=True).step -> jx_adamw_step
+ */
+#ifndef JISHUI_B200_H_
+#define JISHUI_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* jx_stream_t; /* == cudaStream_t */
+
+#define JX_OK 0
+#define JX_ERR_INVALID -1     /* bad argument, shape or alignment */
+#define JX_ERR_UNSUPPORTED -2 /* valid but not implemented for this shape */
+#define JX_ERR_LAUNCH -3      /* CUDA launch / runtime error */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int jx_version(void);
+/* Text of the last error on this host thread ("" if none). */
+const char* jx_last_error(void);
+/* Device-side status word: non-zero when a kernel abandoned work after a
+ * bounded wait expired (code identifies the wait). Reads and optionally clears
+ * it; synchronises the current device. */
+int jx_device_status(int* status_out, int clear);
+
+/* ---- RMSNorm (model_torch.py:12-15, nn.RMSNorm, eps from ModelConfig.norm_eps) ----
+ * Forward: s = x (+ resid if resid != NULL, stored to sum_out as f16);
+ *   rstd[r] = 1/sqrt(mean(s^2) + eps);  y = f16( f16(s*rstd) * gamma ).
+ * x, resid, sum_out, y: f16 [rows, cols] contiguous; gamma f32 [cols]; rstd f32 [rows].
+ * cols must be a multiple of 8 and <= 8192. */
+int jx_rmsnorm_fwd(const void* x, const void* resid, void* sum_out, const float* gamma, void* y, float* rstd,
+                   int64_t rows, int cols, float eps, jx_stream_t stream);
+/* Backward: dx = f16( dresid + f16(d rmsnorm/dx . dy) ) (dresid optional).
+ * dy is f16 [rows, cols]; x is the forward input s; dgamma_part is f32
+ * [nparts, cols] with nparts = jx_rmsnorm_bwd_parts(rows); reduce it with
+ * jx_rmsnorm_dgamma_reduce. */
+int jx_rmsnorm_bwd_parts(int64_t rows);
+int jx_rmsnorm_bwd(const void* dy, const void* x, const float* rstd, const float* gamma, const void* dresid,
+                   void* dx, float* dgamma_part, int64_t rows, int cols, jx_stream_t stream);
+/* dgamma (+)= sum over parts (accumulate != 0 adds to the existing value). */
+int jx_rmsnorm_dgamma_reduce(const float* dgamma_part, int nparts, int cols, float* dgamma, int accumulate,
+                             jx_stream_t stream);
+
+/* ---- Embedding (model_torch.py:89-93): out[t] = table16[ids[t]] ----
+ * Ids outside [0, vocab) produce zero rows and set the device status word. */
+int jx_embed_fwd(const int64_t* ids, int64_t ntok, const void* table16, int64_t vocab, int cols, void* out16,
+                 jx_stream_t stream);
+/* dtable[ids[t]] += f32(dout16[t]) (fp32 atomics). */
+int jx_embed_bwd(const int64_t* ids, int64_t ntok, const void* dout16, int64_t vocab, int cols, float* dtable,
+                 jx_stream_t stream);
+
+/* ---- Dense GEMMs on tcgen05 (fp16 operands, fp32 accumulation in TMEM) ----
+ * Logical product acc[m][n] = sum_k A[m][k] * B[n][k].
+ * a_mn_major = 0: A stored [M][K] (row stride lda); 1: A stored [K][M].
+ * b_mn_major = 0: B stored [N][K] (row stride ldb); 1: B stored [K][N].
+ * All leading dimensions must be multiples of 8, bases 16-byte aligned,
+ * N a multiple of 8. */
+/* C16[m][n] = f16(acc) or, with resid != NULL, f16(resid[m][n] + f16(acc)). */
+int jx_gemm_f16(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major, int M, int N,
+                int K, void* C, int64_t ldc, const void* resid, int64_t ld_resid, jx_stream_t stream);
+/* Fused q/k/v projection with RoPE (model_torch.py:18-25, 41-44): C = [q|k|v] f16
+ * [M, 3*hidden], with the first 2*hidden columns rotated per head_dim-wide
+ * head (half-split pairs) at position (row % seq_len), using tables
+ * cos/sin f32 [seq_len, head_dim/2]. W is the stacked [3*hidden, K] f16 weight. */
+int jx_gemm_qkv_rope(const void* X, int64_t ldx, const void* W, int M, int hidden, int K, void* C, int64_t ldc,
+                     const float* rope_cos, const float* rope_sin, int seq_len, int head_dim, jx_stream_t stream);
+/* SwiGLU forward (model_torch.py:59-60): Wgu is [gate; up] f16 [2F, K];
+ * writes gate = f16(X Wg^T), up = f16(X Wu^T), act = f16(f16(silu(gate)) * up),
+ * each f16 [M, F] with leading dimension ld_out. */
+int jx_gemm_swiglu_fwd(const void* X, int64_t ldx, const void* Wgu, int M, int F, int K, void* gate, void* up,
+                       void* act, int64_t ld_out, jx_stream_t stream);
+/* SwiGLU backward through the down projection: dact = f16(dY Wd) with dY f16
+ * [M, K] and Wd f16 [K, F]; then dgu[:, 0:F] = d gate, dgu[:, F:2F] = d up
+ * (f16 [M, 2F], leading dimension ld_dgu). */
+int jx_gemm_swiglu_bwd(const void* dY, int64_t lddy, const void* Wd, int M, int F, int K, const void* gate,
+                       const void* up, int64_t ld_gu, void* dgu, int64_t ld_dgu, jx_stream_t stream);
+/* Weight gradient: G[n][k] (+)= f32( f16( sum_t dY[t][n] * X[t][k] ) ) with
+ * dY f16 [T, N], X f16 [T, K], G f32 [N, K] (leading dimension ldg).
+ * The product is rounded to f16 before it is added, as an fp16 autocast
+ * Linear's weight gradient is. `splits` > 1 splits the T reduction across
+ * CTAs; it needs `workspace` of jx_gemm_wgrad_workspace_bytes(N, K, splits). */
+int64_t jx_gemm_wgrad_workspace_bytes(int N, int K, int splits);
+int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_t ldx, int T, int N, int K, float* G,
+                  int64_t ldg, int accumulate, int splits, void* workspace, jx_stream_t stream);
+
+/* ---- Causal attention (model_torch.py:48, SDPA is_causal=True) ----
+ * qkv: f16 [B*T, 3*H*D] rows (q | k | v, head h at column h*D of each part).
+ * out: f16 [B*T, H*D]. lse: f32 [B, H, T] (natural-log logsumexp of the scaled scores). */
+int jx_attn_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int D, float scale,
+                jx_stream_t stream);
+/* Backward: writes dqkv f16 [B*T, 3*H*D]; delta is f32 [B, H, T] scratch.
+ * If rope_cos/rope_sin are non-NULL the q/k gradients are rotated back
+ * through RoPE (the inverse rotation) before they are stored. */
+int jx_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, float* delta, void* dqkv,
+                int B, int T, int H, int D, float scale, const float* rope_cos, const float* rope_sin,
+                jx_stream_t stream);
+
+/* ---- Cross-entropy over f16 logits (model_torch.py:102-104) ----
+ * Per row: lse = log(sum exp(logit)), loss = lse - logit[target]; rows whose
+ * target == ignore_index give loss 0 and are excluded from the mean. */
+int jx_ce_fwd(const void* logits16, int64_t rows, int vocab, int64_t ld, const int64_t* targets, int64_t ignore_index,
+              float* lse, float* row_loss, jx_stream_t stream);
+/* loss_sum_count[0] = sum of row losses, [1] = number of counted rows
+ * (deterministic order); accumulate != 0 adds to the existing values. */
+int jx_ce_loss(const float* row_loss, const int64_t* targets, int64_t ignore_index, int64_t rows,
+               float* loss_sum_count, int accumulate, jx_stream_t stream);
+/* In place: logits16 <- f16( (exp(logit - lse) - onehot(target)) * g ),
+ * g = (*grad_loss) / (*count), i.e. the gradient of mean CE scaled by the
+ * incoming gradient of the loss. */
+int jx_ce_bwd(void* logits16, int64_t rows, int vocab, int64_t ld, const int64_t* targets, int64_t ignore_index,
+              const float* lse, const float* grad_loss, const float* count, jx_stream_t stream);
+
+/* ---- GradScaler unscale + inf check + global norm, then AdamW ----
+ * Stats over a flat gradient buffer (grad_is_f16 selects f16 or f32 input):
+ * partial[b] = sum over the block's slice of (g*inv_scale)^2, found_inf set to 1
+ * if any element is not finite. nparts = jx_grad_stats_parts(n). */
+int jx_grad_stats_parts(int64_t n);
+int jx_grad_stats(const void* grad, int grad_is_f16, int64_t n, const float* inv_scale, float* partial,
+                  float* found_inf, jx_stream_t stream);
+/* total_norm = sqrt(sum partial); clip = min(max_norm/(total_norm+1e-6), 1)
+ * (clip_grad_norm_ semantics; max_norm <= 0 disables clipping: clip = 1).
+ * out[0] = total_norm, out[1] = clip coefficient. */
+int jx_grad_finalize(const float* partial, int nparts, float max_norm, float* out, jx_stream_t stream);
+/* One decoupled-weight-decay Adam step over flat buffers, skipped entirely
+ * (no writes) when *found_inf != 0. Gradient used: (g * inv_scale) * clip.
+ * step_count: f32 per-update step number (already incremented) used for the
+ * bias corrections. p16 (optional) receives f16(p_new). */
+int jx_adamw_step(float* p, const void* grad, int grad_is_f16, float* m, float* v, void* p16, int64_t n,
+                  const float* inv_scale, const float* clip, const float* found_inf, float lr, float beta1,
+                  float beta2, float eps, float weight_decay, float step_count, jx_stream_t stream);
+/* GradScaler.update(): if found_inf: scale *= backoff, tracker = 0; else
+ * tracker += 1 and at growth_interval scale *= growth, tracker = 0. */
+int jx_scaler_update(float* scale, int* growth_tracker, const float* found_inf, float growth_factor,
+                     float backoff_factor, int growth_interval, jx_stream_t stream);
+
+/* ---- Utilities ---- */
+/* dst16[i] = f16(src32[i]). */
+int jx_cast_f32_f16(const float* src, void* dst16, int64_t n, jx_stream_t stream);
+/* dst16 [cols, rows] = transpose(src16 [rows, cols]). */
+int jx_transpose_f16(const void* src, void* dst, int64_t rows, int64_t cols, jx_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JISHUI_B200_H_ */

@@ -1,0 +1,646 @@
+// Persistent tcgen05 GEMM for the Jishui decoder's dense contractions.
+//
+// acc[m][n] = sum_k A[m][k] * B[n][k]; fp16 operands staged by TMA into
+// 128B-swizzled shared memory, fp32 accumulators in tensor memory (TMEM).
+// One CTA per SM (persistent), 192 threads:
+//   warp 0      TMA producer (one elected lane) filling a 4-stage ring,
+//   warp 1      TMEM allocator + MMA issuer (one elected lane),
+//   warps 2..5  epilogue: tcgen05.ld from TMEM -> fused math -> global stores.
+// The accumulator is double-buffered in TMEM (2 x 256 columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Both operands may be K-major or MN-major in global memory; MN-major
+// operands (the dgrad / wgrad products of backward) are consumed directly
+// through the descriptor's major bit instead of being transposed in HBM.
+//
+// Fused epilogues (reference call sites in Midstream-LLM):
+//   kF16      plain / residual add         model_torch.py:49,60,72-73,98
+//   kRope     q|k|v projection + RoPE      model_torch.py:18-25,41-44
+//   kSwigluF  gate|up projection + SwiGLU  model_torch.py:59-60
+//   kSwigluB  down dgrad + SwiGLU backward (autograd of model_torch.py:60)
+//   kWgrad    weight gradient in f32, rounded through f16 as an fp16
+//             autocast Linear's weight gradient is before it reaches .grad
+#include <math.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "jx_common.cuh"
+#include "jx_host.h"
+
+namespace jx {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kABytes = BM * BK * 2;  // 16 KiB
+constexpr uint32_t kBBytes = BN * BK * 2;  // 32 KiB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemCols = 512;
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + STAGES * kStageBytes + 256 /*barriers*/;
+
+enum Epi : int { kF16 = 0, kRope = 1, kSwigluF = 2, kSwigluB = 3, kWgrad = 4 };
+
+struct Params {
+  int M, N, K;
+  int tiles_m, tiles_n, splits, kb_per_split, num_kb;
+  int swiglu_F;  // kSwigluF: row offset of the up half inside B; kSwigluB: F
+  // outputs
+  __half* C;
+  int64_t ldc;
+  const __half* resid;
+  int64_t ld_resid;
+  __half* out1;
+  __half* out2;
+  int64_t ld_out;
+  const __half* aux0;
+  const __half* aux1;
+  int64_t ld_aux;
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_seq;
+  int rope_cols;
+  float* G;
+  int64_t ldg;
+  int accumulate;
+  float* ws;
+  int* status;
+};
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                         int code) {
+  long long start = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      if (*abort_flag) return false;
+      if (clock64() - start > (1ll << 32)) {
+        *abort_flag = 1;
+        if (status) atomicExch(status, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& mb, int& nb, int& s) {
+  const int per_split = p.tiles_m * p.tiles_n;
+  s = t / per_split;
+  int tt = t - s * per_split;
+  // Grouped raster: 16 M-blocks share each sweep over N for L2 reuse of B.
+  constexpr int GM = 16;
+  const int group_span = GM * p.tiles_n;
+  const int g = tt / group_span;
+  const int r = tt - g * group_span;
+  const int rows = min(GM, p.tiles_m - g * GM);
+  mb = g * GM + r % rows;
+  nb = r / rows;
+}
+
+__device__ __forceinline__ float h2f_round(float x) { return __half2float(__float2half_rn(x)); }
+
+// Store 32 consecutive fp32 values of row `row` starting at column `col` as fp16.
+__device__ __forceinline__ void store_row32_f16(__half* base, int64_t ld, int row, int col, int M, int N,
+                                                const float (&v)[32]) {
+  if (row >= M) return;
+  __half* dst = base + (int64_t)row * ld + col;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (col + g * 8 + 8 <= N) {
+      half8 h;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h.h[j] = __floats2half2_rn(v[g * 8 + 2 * j], v[g * 8 + 2 * j + 1]);
+      *reinterpret_cast<half8*>(dst + g * 8) = h;
+    }
+  }
+}
+
+__device__ __forceinline__ void load_row32_f16(const __half* base, int64_t ld, int row, int col, int M, int N,
+                                               float (&v)[32]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (row < M && col + g * 8 + 8 <= N) {
+      half8 h = *reinterpret_cast<const half8*>(base + (int64_t)row * ld + col + g * 8);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(h.h[j]);
+        v[g * 8 + 2 * j] = f.x;
+        v[g * 8 + 2 * j + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[g * 8 + j] = 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ void tmem_load32f(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, 1.0f + expf(-x)); }
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, int quarter, int lane, int mb, int nb,
+                                              int split) {
+  const int row = mb * BM + quarter * 32 + lane;
+  const uint32_t tl = tacc + (static_cast<uint32_t>(quarter * 32) << 16);
+  if constexpr (EPI == kF16) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = nb * BN + c * 32;
+      if (col >= p.N) break;
+      float v[32];
+      tmem_load32f(tl + c * 32, v);
+      if (p.resid) {
+        float r[32];
+        load_row32_f16(p.resid, p.ld_resid, row, col, p.M, p.N, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = r[i] + h2f_round(v[i]);
+      }
+      store_row32_f16(p.C, p.ldc, row, col, p.M, p.N, v);
+    }
+  } else if constexpr (EPI == kRope) {
+    const int pos = p.rope_seq > 0 ? row % p.rope_seq : 0;
+#pragma unroll 1
+    for (int h = 0; h < BN / 64; ++h) {
+      const int col = nb * BN + h * 64;
+      if (col >= p.N) break;
+      float a[32], b[32];
+      tmem_load32f(tl + h * 64, a);
+      tmem_load32f(tl + h * 64 + 32, b);
+      if (col < p.rope_cols && row < p.M) {
+        const float* cs = p.rope_cos + (int64_t)pos * 32;
+        const float* sn = p.rope_sin + (int64_t)pos * 32;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x0 = h2f_round(a[i]);
+          const float x1 = h2f_round(b[i]);
+          const float c_ = __ldg(cs + i), s_ = __ldg(sn + i);
+          a[i] = __fsub_rn(__fmul_rn(x0, c_), __fmul_rn(x1, s_));
+          b[i] = __fadd_rn(__fmul_rn(x0, s_), __fmul_rn(x1, c_));
+        }
+      }
+      store_row32_f16(p.C, p.ldc, row, col, p.M, p.N, a);
+      store_row32_f16(p.C, p.ldc, row, col + 32, p.M, p.N, b);
+    }
+  } else if constexpr (EPI == kSwigluF) {
+    const int F = p.swiglu_F;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      const int col = nb * 128 + c * 32;
+      if (col >= F) break;
+      float g[32], u[32];
+      tmem_load32f(tl + c * 32, g);
+      tmem_load32f(tl + 128 + c * 32, u);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        g[i] = h2f_round(g[i]);
+        u[i] = h2f_round(u[i]);
+      }
+      store_row32_f16(p.C, p.ld_out, row, col, p.M, F, g);
+      store_row32_f16(p.out1, p.ld_out, row, col, p.M, F, u);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) g[i] = __fmul_rn(h2f_round(silu_f(g[i])), u[i]);
+      store_row32_f16(p.out2, p.ld_out, row, col, p.M, F, g);
+    }
+  } else if constexpr (EPI == kSwigluB) {
+    const int F = p.swiglu_F;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = nb * BN + c * 32;
+      if (col >= F) break;
+      float d[32], g[32], u[32];
+      tmem_load32f(tl + c * 32, d);
+      load_row32_f16(p.aux0, p.ld_aux, row, col, p.M, F, g);
+      load_row32_f16(p.aux1, p.ld_aux, row, col, p.M, F, u);
+      float du[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float d16 = h2f_round(d[i]);
+        const float s16 = h2f_round(silu_f(g[i]));
+        du[i] = __fmul_rn(d16, s16);
+        const float ds = h2f_round(__fmul_rn(d16, u[i]));
+        const float sig = __fdiv_rn(1.0f, 1.0f + expf(-g[i]));
+        d[i] = __fmul_rn(__fmul_rn(ds, sig), 1.0f + __fmul_rn(g[i], 1.0f - sig));
+      }
+      store_row32_f16(p.C, p.ldc, row, col, p.M, F, d);
+      store_row32_f16(p.C + F, p.ldc, row, col, p.M, F, du);
+    }
+  } else if constexpr (EPI == kWgrad) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = nb * BN + c * 32;
+      if (col >= p.N) break;
+      float v[32];
+      tmem_load32f(tl + c * 32, v);
+      if (row >= p.M) continue;
+      if (p.splits > 1) {
+        float* dst = p.ws + ((int64_t)split * p.M + row) * p.N + col;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          if (col + g * 4 + 4 <= p.N)
+            *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
+      } else {
+        float* dst = p.G + (int64_t)row * p.ldg + col;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          if (col + g * 4 + 4 <= p.N) {
+            float4 o = make_float4(h2f_round(v[g * 4]), h2f_round(v[g * 4 + 1]), h2f_round(v[g * 4 + 2]),
+                                   h2f_round(v[g * 4 + 3]));
+            if (p.accumulate) {
+              float4 old = *reinterpret_cast<float4*>(dst + g * 4);
+              o.x += old.x;
+              o.y += old.y;
+              o.z += old.z;
+              o.w += old.w;
+            }
+            *reinterpret_cast<float4*>(dst + g * 4) = o;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int EPI, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.tiles_m * p.tiles_n * p.splits;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb, s;
+        tile_coords(p, t, mb, nb, s);
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const uint32_t stage = it % STAGES;
+          const uint32_t parity = ((it / STAGES) & 1u) ^ 1u;
+          if (!wait_bar(&empty[stage], parity, abort_flag, p.status, kStatusGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], kStageBytes);
+          uint8_t* a_dst = smA + stage * kABytes;
+          uint8_t* b_dst = smB + stage * kBBytes;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, mb * BM);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], mb * BM, kb * BK);
+            tma_load_2d(a_dst + 8192, &tmA, &full[stage], mb * BM + 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            if constexpr (EPI == kSwigluF) {
+              tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, nb * 128);
+              tma_load_2d(b_dst + 16384, &tmB, &full[stage], kb * BK, p.swiglu_F + nb * 128);
+            } else {
+              tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, nb * BN);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], nb * BN + j * 64, kb * BK);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(BM, BN, A_MN, B_MN);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        int mb, nb, s;
+        tile_coords(p, t, mb, nb, s);
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        const int acc = local & 1;
+        if (!wait_bar(&acc_empty[acc], ((local >> 1) & 1) ^ 1, abort_flag, p.status, kStatusGemmMmaWait)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const uint32_t stage = it % STAGES;
+          if (!wait_bar(&full[stage], (it / STAGES) & 1u, abort_flag, p.status, kStatusGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smA + stage * kABytes);
+          const uint32_t b_base = smem_u32(smB + stage * kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? smem_desc_sw128(a_base + k * 2048, 8192, 1024)
+                                        : smem_desc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_base + k * 2048, 8192, 1024)
+                                        : smem_desc_sw128(b_base + k * 32, 16, 1024);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+        }
+        if (ok) umma_commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      int mb, nb, s;
+      tile_coords(p, t, mb, nb, s);
+      const int acc = local & 1;
+      if (!wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
+      tc_fence_after();
+      epilogue_tile<EPI>(p, tmem_base + acc * BN, quarter, lane, mb, nb, s);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Split-K reduction for the weight gradient: G (+)= f32(f16(sum_s ws[s])).
+__global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, float* __restrict__ G,
+                                    int64_t ldg, int accumulate) {
+  const int64_t total4 = (int64_t)M * N / 4;
+  const int64_t plane = (int64_t)M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total4; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i * 4;
+    const int row = (int)(e / N);
+    const int col = (int)(e - (int64_t)row * N);
+    float4 acc = *reinterpret_cast<const float4*>(ws + e);
+    for (int s = 1; s < splits; ++s) {
+      float4 v = *reinterpret_cast<const float4*>(ws + s * plane + e);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    float* dst = G + (int64_t)row * ldg + col;
+    float4 o = make_float4(h2f_round(acc.x), h2f_round(acc.y), h2f_round(acc.z), h2f_round(acc.w));
+    if (accumulate) {
+      float4 old = *reinterpret_cast<float4*>(dst);
+      o.x += old.x;
+      o.y += old.y;
+      o.z += old.z;
+      o.w += old.w;
+    }
+    *reinterpret_cast<float4*>(dst) = o;
+  }
+}
+
+}  // namespace gemm
+
+// ---------------------------------------------------------------------------
+// TMA descriptor construction through the driver entry point (no -lcuda).
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                   uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+namespace gemm {
+
+template <int EPI, bool A_MN, bool B_MN>
+static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params p, cudaStream_t stream,
+                  const char* name) {
+  JX_CHECK_ARG(A && B, "%s: NULL operand", name);
+  JX_CHECK_ARG(p.M > 0 && p.N > 0 && p.K > 0, "%s: empty shape M=%d N=%d K=%d", name, p.M, p.N, p.K);
+  JX_CHECK_ARG(aligned16(A) && aligned16(B), "%s: operands must be 16-byte aligned", name);
+  JX_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0, "%s: leading dimensions must be multiples of 8 (lda=%lld ldb=%lld)",
+               name, (long long)lda, (long long)ldb);
+  CUtensorMap ta, tb;
+  bool ok;
+  if (!A_MN)
+    ok = make_tmap_f16(&ta, A, p.K, p.M, lda, BK, BM);
+  else
+    ok = make_tmap_f16(&ta, A, p.M, p.K, lda, 64, BK);
+  JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for A", name);
+  const int b_rows = (EPI == kSwigluF) ? 2 * p.swiglu_F : p.N;
+  if (!B_MN)
+    ok = make_tmap_f16(&tb, B, p.K, b_rows, ldb, BK, (EPI == kSwigluF) ? 128 : BN);
+  else
+    ok = make_tmap_f16(&tb, B, b_rows, p.K, ldb, 64, BK);
+  JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for B", name);
+
+  p.tiles_m = (p.M + BM - 1) / BM;
+  p.tiles_n = (EPI == kSwigluF) ? (p.swiglu_F + 127) / 128 : (p.N + BN - 1) / BN;
+  p.num_kb = (p.K + BK - 1) / BK;
+  if (p.splits < 1) p.splits = 1;
+  if (p.splits > p.num_kb) p.splits = p.num_kb;
+  p.kb_per_split = (p.num_kb + p.splits - 1) / p.splits;
+  p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+  p.status = status_ptr();
+
+  static bool attr_set = false;  // per template instantiation
+  if (!attr_set) {
+    JX_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<EPI, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kSmemBytes),
+                name);
+    attr_set = true;
+  }
+  const int tiles = p.tiles_m * p.tiles_n * p.splits;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_kernel<EPI, A_MN, B_MN><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  JX_CHECK_LAUNCH(name);
+  return JX_OK;
+}
+
+static Params base_params(int M, int N, int K) {
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.splits = 1;
+  return p;
+}
+
+}  // namespace gemm
+}  // namespace jx
+
+using namespace jx;
+using namespace jx::gemm;
+
+extern "C" int jx_gemm_f16(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
+                           int M, int N, int K, void* C, int64_t ldc, const void* resid, int64_t ld_resid,
+                           jx_stream_t stream) {
+  JX_CHECK_ARG(C && aligned16(C) && ldc % 8 == 0 && N % 8 == 0, "jx_gemm_f16: C must be 16B aligned, ldc%%8==0, N%%8==0");
+  JX_CHECK_ARG(!resid || (aligned16(resid) && ld_resid % 8 == 0), "jx_gemm_f16: bad residual");
+  Params p = base_params(M, N, K);
+  p.C = static_cast<__half*>(C);
+  p.ldc = ldc;
+  p.resid = static_cast<const __half*>(resid);
+  p.ld_resid = ld_resid;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (!a_mn_major && !b_mn_major) return launch<kF16, false, false>(A, lda, B, ldb, p, s, "jx_gemm_f16");
+  if (!a_mn_major && b_mn_major) return launch<kF16, false, true>(A, lda, B, ldb, p, s, "jx_gemm_f16");
+  if (a_mn_major && !b_mn_major) return launch<kF16, true, false>(A, lda, B, ldb, p, s, "jx_gemm_f16");
+  return launch<kF16, true, true>(A, lda, B, ldb, p, s, "jx_gemm_f16");
+}
+
+extern "C" int jx_gemm_qkv_rope(const void* X, int64_t ldx, const void* W, int M, int hidden, int K, void* C,
+                                int64_t ldc, const float* rope_cos, const float* rope_sin, int seq_len,
+                                int head_dim, jx_stream_t stream) {
+  JX_CHECK_ARG(head_dim == 64, "jx_gemm_qkv_rope: head_dim must be 64 (got %d)", head_dim);
+  JX_CHECK_ARG(hidden % 64 == 0, "jx_gemm_qkv_rope: hidden must be a multiple of 64");
+  JX_CHECK_ARG(rope_cos && rope_sin && seq_len > 0, "jx_gemm_qkv_rope: missing RoPE tables");
+  JX_CHECK_ARG(C && aligned16(C) && ldc % 8 == 0, "jx_gemm_qkv_rope: bad output");
+  Params p = base_params(M, 3 * hidden, K);
+  p.C = static_cast<__half*>(C);
+  p.ldc = ldc;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
+  p.rope_seq = seq_len;
+  p.rope_cols = 2 * hidden;
+  return launch<kRope, false, false>(X, ldx, W, K, p, reinterpret_cast<cudaStream_t>(stream), "jx_gemm_qkv_rope");
+}
+
+extern "C" int jx_gemm_swiglu_fwd(const void* X, int64_t ldx, const void* Wgu, int M, int F, int K, void* gate,
+                                  void* up, void* act, int64_t ld_out, jx_stream_t stream) {
+  JX_CHECK_ARG(gate && up && act && aligned16(gate) && aligned16(up) && aligned16(act),
+               "jx_gemm_swiglu_fwd: outputs must be 16-byte aligned");
+  JX_CHECK_ARG(F % 8 == 0 && ld_out % 8 == 0, "jx_gemm_swiglu_fwd: F and ld_out must be multiples of 8");
+  Params p = base_params(M, 2 * F, K);
+  p.swiglu_F = F;
+  p.C = static_cast<__half*>(gate);
+  p.out1 = static_cast<__half*>(up);
+  p.out2 = static_cast<__half*>(act);
+  p.ld_out = ld_out;
+  return launch<kSwigluF, false, false>(X, ldx, Wgu, K, p, reinterpret_cast<cudaStream_t>(stream),
+                                        "jx_gemm_swiglu_fwd");
+}
+
+extern "C" int jx_gemm_swiglu_bwd(const void* dY, int64_t lddy, const void* Wd, int M, int F, int K, const void* gate,
+                                  const void* up, int64_t ld_gu, void* dgu, int64_t ld_dgu, jx_stream_t stream) {
+  JX_CHECK_ARG(gate && up && dgu && aligned16(gate) && aligned16(up) && aligned16(dgu),
+               "jx_gemm_swiglu_bwd: buffers must be 16-byte aligned");
+  JX_CHECK_ARG(F % 8 == 0 && ld_gu % 8 == 0 && ld_dgu % 8 == 0, "jx_gemm_swiglu_bwd: F, ld_gu, ld_dgu must be multiples of 8");
+  Params p = base_params(M, F, K);
+  p.swiglu_F = F;
+  p.C = static_cast<__half*>(dgu);
+  p.ldc = ld_dgu;
+  p.aux0 = static_cast<const __half*>(gate);
+  p.aux1 = static_cast<const __half*>(up);
+  p.ld_aux = ld_gu;
+  // dact[m][f] = sum_k dY[m][k] * Wd[k][f]: B is Wd read MN-major.
+  return launch<kSwigluB, false, true>(dY, lddy, Wd, F, p, reinterpret_cast<cudaStream_t>(stream),
+                                       "jx_gemm_swiglu_bwd");
+}
+
+extern "C" int64_t jx_gemm_wgrad_workspace_bytes(int N, int K, int splits) {
+  if (splits <= 1) return 0;
+  return (int64_t)splits * N * K * (int64_t)sizeof(float);
+}
+
+extern "C" int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_t ldx, int T, int N, int K, float* G,
+                             int64_t ldg, int accumulate, int splits, void* workspace, jx_stream_t stream) {
+  JX_CHECK_ARG(G && ((uintptr_t)G & 15) == 0 && ldg % 4 == 0 && K % 8 == 0, "jx_gemm_wgrad: bad gradient buffer");
+  JX_CHECK_ARG(splits >= 1, "jx_gemm_wgrad: splits must be >= 1");
+  JX_CHECK_ARG(splits == 1 || (workspace && ((uintptr_t)workspace & 15) == 0),
+               "jx_gemm_wgrad: splits > 1 needs a 16-byte aligned workspace");
+  // acc[n][k] = sum_t dY[t][n] * X[t][k]: both operands MN-major, reduction over tokens.
+  Params p = base_params(N, K, T);
+  p.G = G;
+  p.ldg = ldg;
+  p.accumulate = accumulate;
+  p.splits = splits;
+  p.ws = static_cast<float*>(workspace);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Clamp the split count exactly as launch() does so the reduction sees the same value.
+  const int num_kb = (T + BK - 1) / BK;
+  int sp = splits > num_kb ? num_kb : splits;
+  const int per = (num_kb + sp - 1) / sp;
+  sp = (num_kb + per - 1) / per;
+  p.splits = sp;
+  int rc = launch<kWgrad, true, true>(dY, lddy, X, ldx, p, s, "jx_gemm_wgrad");
+  if (rc != JX_OK || sp == 1) return rc;
+  const int64_t total4 = (int64_t)N * K / 4;
+  int blocks = (int)((total4 + 255) / 256);
+  if (blocks > num_sms() * 8) blocks = num_sms() * 8;
+  wgrad_reduce_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(workspace), sp, N, K, G, ldg, accumulate);
+  JX_CHECK_LAUNCH("jx_gemm_wgrad: reduce");
+  return JX_OK;
+}

@@ -1,0 +1,71 @@
+// Host-side plumbing shared by all entry points: per-thread error text,
+// the device status word kernels set when a bounded wait expires, SM count.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "jx_common.cuh"
+#include "jx_host.h"
+
+namespace jx {
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+// One status word per device. Kernels that abandon work after a bounded
+// wait write a non-zero code here; jx_device_status() reads it back.
+static __device__ int g_device_status;
+
+static std::mutex g_mu;
+static int* g_status_ptr[64];
+static int g_sms[64];
+
+int* status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+int num_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_sms[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sms[dev] = n;
+  }
+  return g_sms[dev];
+}
+
+}  // namespace jx
+
+extern "C" int jx_version(void) { return 100; }
+
+extern "C" const char* jx_last_error(void) { return jx::g_last_error; }
+
+extern "C" int jx_device_status(int* status_out, int clear) {
+  JX_CHECK_ARG(status_out != nullptr, "jx_device_status: status_out is NULL");
+  JX_CUDA_TRY(cudaDeviceSynchronize(), "jx_device_status: synchronize");
+  int v = 0;
+  JX_CUDA_TRY(cudaMemcpyFromSymbol(&v, jx::g_device_status, sizeof(int)), "jx_device_status: read");
+  *status_out = v;
+  if (clear) {
+    int z = 0;
+    JX_CUDA_TRY(cudaMemcpyToSymbol(jx::g_device_status, &z, sizeof(int)), "jx_device_status: clear");
+  }
+  return JX_OK;
+}

@@ -1,0 +1,268 @@
+// RMSNorm forward/backward with optional residual-add fusion.
+//
+// Follows nn.RMSNorm as the reference decoder uses it under fp16 autocast
+// (Midstream-LLM src/jishui/model_torch.py:12-15, 72-73): the residual
+// stream is fp16, the statistics are computed in fp32, the normalised value is
+// rounded to fp16 before the fp32 gain multiplies it, and the result feeds an
+// fp16 GEMM (so it is rounded to fp16 once more here).
+//
+// One warp per row; each lane owns NV 8-element (16-byte) vectors, so a row
+// of `cols` fp16 values is read once with coalesced 16-byte loads and kept in
+// registers. HBM traffic per row: fwd 2*cols*2 bytes (+2*cols*2 with the
+// residual), bwd 3*cols*2 bytes (+cols*2 with the residual gradient).
+#include "jx_common.cuh"
+#include "jx_host.h"
+
+namespace jx {
+namespace rms {
+
+constexpr int kWarps = 8;
+constexpr int kMaxParts = 296;
+
+__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
+  half8 h = *reinterpret_cast<const half8*>(p);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 f = __half22float2(h.h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__half* p, const float (&v)[8]) {
+  half8 h;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h.h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+  *reinterpret_cast<half8*>(p) = h;
+}
+
+__device__ __forceinline__ float r16(float x) { return __half2float(__float2half_rn(x)); }
+
+template <int NV>
+__global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_kernel(const __half* __restrict__ x,
+                                                                  const __half* __restrict__ resid,
+                                                                  __half* __restrict__ sum_out,
+                                                                  const float* __restrict__ gamma,
+                                                                  __half* __restrict__ y, float* __restrict__ rstd,
+                                                                  int64_t rows, int cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const __half* xr = x + row * cols;
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < cols) {
+      load8(xr + c, v[i]);
+      if (resid) {
+        float r[8];
+        load8(resid + row * cols + c, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = r16(v[i][j] + r[j]);
+        store8(sum_out + row * cols + c, v[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = warp_sum(ss);
+  const float rs = 1.0f / sqrtf(ss / (float)cols + eps);
+  if (lane == 0) rstd[row] = rs;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < cols) {
+      float o[8];
+      const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+      const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = r16(v[i][j] * rs) * g[j];
+      store8(y + row * cols + c, o);
+    }
+  }
+}
+
+// dx = f16(dresid + f16(rstd * (gh - xhat * mean(gh * xhat)))), gh = f16(dy * gamma),
+// xhat = x * rstd; dgamma partial += dy * f16(xhat).
+template <int NV>
+__global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __half* __restrict__ dy,
+                                                                  const __half* __restrict__ x,
+                                                                  const float* __restrict__ rstd,
+                                                                  const float* __restrict__ gamma,
+                                                                  const __half* __restrict__ dresid,
+                                                                  __half* __restrict__ dx,
+                                                                  float* __restrict__ dgamma_part, int64_t rows,
+                                                                  int cols) {
+  extern __shared__ float red[];  // [kWarps][cols]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float dg[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dg[i][j] = 0.f;
+
+  for (int64_t row = blockIdx.x * (int64_t)kWarps + warp; row < rows; row += (int64_t)gridDim.x * kWarps) {
+    const float rs = rstd[row];
+    float xv[NV][8], gv[NV][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < cols) {
+        float d[8];
+        load8(dy + row * cols + c, d);
+        load8(x + row * cols + c, xv[i]);
+        const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+        const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = xv[i][j] * rs;
+          dg[i][j] += d[j] * r16(xh);
+          gv[i][j] = r16(d[j] * g[j]);
+          dot += gv[i][j] * xh;
+        }
+      }
+    }
+    dot = warp_sum(dot) / (float)cols;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < cols) {
+        float o[8];
+        float r[8];
+        if (dresid) load8(dresid + row * cols + c, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = xv[i][j] * rs;
+          o[j] = r16(rs * (gv[i][j] - xh * dot));
+          if (dresid) o[j] += r[j];
+        }
+        store8(dx + row * cols + c, o);
+      }
+    }
+  }
+  // Block reduction of the dgamma partials across warps.
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < cols)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red[warp * cols + c + j] = dg[i][j];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red[w * cols + c];
+    dgamma_part[(int64_t)blockIdx.x * cols + c] = s;
+  }
+}
+
+__global__ void dgamma_reduce_kernel(const float* __restrict__ part, int nparts, int cols, float* __restrict__ dgamma,
+                                     int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += part[(int64_t)p * cols + c];
+  dgamma[c] = accumulate ? dgamma[c] + s : s;
+}
+
+template <template <int> class K>
+struct Dispatch;
+
+}  // namespace rms
+}  // namespace jx
+
+using namespace jx;
+using namespace jx::rms;
+
+extern "C" int jx_rmsnorm_bwd_parts(int64_t rows) {
+  int64_t b = (rows + kWarps - 1) / kWarps;
+  return (int)(b < kMaxParts ? (b < 1 ? 1 : b) : kMaxParts);
+}
+
+#define JX_RMS_NV_CASES(X) X(1) X(2) X(3) X(4) X(5) X(6) X(8) X(12) X(16)
+
+static int pick_nv(int cols) {
+  const int nv = (cols + 255) / 256;
+  const int allowed[] = {1, 2, 3, 4, 5, 6, 8, 12, 16};
+  for (int a : allowed)
+    if (nv <= a) return a;
+  return -1;
+}
+
+extern "C" int jx_rmsnorm_fwd(const void* x, const void* resid, void* sum_out, const float* gamma, void* y,
+                              float* rstd, int64_t rows, int cols, float eps, jx_stream_t stream) {
+  JX_CHECK_ARG(x && gamma && y && rstd, "jx_rmsnorm_fwd: NULL argument");
+  JX_CHECK_ARG(rows > 0 && cols > 0 && cols % 8 == 0 && cols <= 4096, "jx_rmsnorm_fwd: cols must be a multiple of 8 in (0, 4096] (got %d)", cols);
+  JX_CHECK_ARG(!resid || sum_out, "jx_rmsnorm_fwd: residual input needs sum_out");
+  JX_CHECK_ARG(aligned16(x) && aligned16(y) && aligned16(gamma) && (!resid || (aligned16(resid) && aligned16(sum_out))),
+               "jx_rmsnorm_fwd: buffers must be 16-byte aligned");
+  const int nv = pick_nv(cols);
+  const unsigned grid = (unsigned)((rows + kWarps - 1) / kWarps);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* rh = static_cast<const __half*>(resid);
+  __half* sh = static_cast<__half*>(sum_out);
+  __half* yh = static_cast<__half*>(y);
+  switch (nv) {
+#define X(N)                                                                                       \
+  case N:                                                                                          \
+    rmsnorm_fwd_kernel<N><<<grid, kWarps * 32, 0, s>>>(xh, rh, sh, gamma, yh, rstd, rows, cols, eps); \
+    break;
+    JX_RMS_NV_CASES(X)
+#undef X
+    default:
+      jx::set_error("jx_rmsnorm_fwd: unsupported cols %d", cols);
+      return JX_ERR_UNSUPPORTED;
+  }
+  JX_CHECK_LAUNCH("jx_rmsnorm_fwd");
+  return JX_OK;
+}
+
+extern "C" int jx_rmsnorm_bwd(const void* dy, const void* x, const float* rstd, const float* gamma, const void* dresid,
+                              void* dx, float* dgamma_part, int64_t rows, int cols, jx_stream_t stream) {
+  JX_CHECK_ARG(dy && x && rstd && gamma && dx && dgamma_part, "jx_rmsnorm_bwd: NULL argument");
+  JX_CHECK_ARG(rows > 0 && cols > 0 && cols % 8 == 0 && cols <= 4096, "jx_rmsnorm_bwd: cols must be a multiple of 8 in (0, 4096]");
+  JX_CHECK_ARG(aligned16(dy) && aligned16(x) && aligned16(dx) && aligned16(gamma) && (!dresid || aligned16(dresid)),
+               "jx_rmsnorm_bwd: buffers must be 16-byte aligned");
+  const int nv = pick_nv(cols);
+  const int grid = jx_rmsnorm_bwd_parts(rows);
+  const size_t smem = (size_t)kWarps * cols * sizeof(float);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __half* dyh = static_cast<const __half*>(dy);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* drh = static_cast<const __half*>(dresid);
+  __half* dxh = static_cast<__half*>(dx);
+  switch (nv) {
+#define X(N)                                                                                     \
+  case N:                                                                                        \
+    if (smem > 48 * 1024)                                                                        \
+      cudaFuncSetAttribute(rmsnorm_bwd_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                           (int)smem);                                                           \
+    rmsnorm_bwd_kernel<N><<<grid, kWarps * 32, smem, s>>>(dyh, xh, rstd, gamma, drh, dxh, dgamma_part, rows, \
+                                                          cols);                                 \
+    break;
+    JX_RMS_NV_CASES(X)
+#undef X
+    default:
+      jx::set_error("jx_rmsnorm_bwd: unsupported cols %d", cols);
+      return JX_ERR_UNSUPPORTED;
+  }
+  JX_CHECK_LAUNCH("jx_rmsnorm_bwd");
+  return JX_OK;
+}
+
+extern "C" int jx_rmsnorm_dgamma_reduce(const float* dgamma_part, int nparts, int cols, float* dgamma, int accumulate,
+                                        jx_stream_t stream) {
+  JX_CHECK_ARG(dgamma_part && dgamma && nparts > 0 && cols > 0, "jx_rmsnorm_dgamma_reduce: bad argument");
+  dgamma_reduce_kernel<<<(cols + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      dgamma_part, nparts, cols, dgamma, accumulate);
+  JX_CHECK_LAUNCH("jx_rmsnorm_dgamma_reduce");
+  return JX_OK;
+}

@@ -1,0 +1,264 @@
+"""Tensor-level wrappers over the C ABI.
+
+Every function takes CUDA tensors, validates dtype / device / layout, and
+launches on torch's current stream. Outputs are allocated here (by torch's
+caching allocator) unless passed in. There is no CPU path: a CPU tensor or a
+missing library raises.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+F16, F32, I64 = torch.float16, torch.float32, torch.int64
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _check(t: torch.Tensor, dtype: torch.dtype, name: str, contiguous: bool = True) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (the Jishui B200 kernels have no CPU path)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+# ---------------------------------------------------------------- RMSNorm
+def rmsnorm_fwd(x: torch.Tensor, gamma: torch.Tensor, eps: float, resid: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, sum_out: torch.Tensor | None = None):
+    """Returns (y, rstd, s) where s = x (+ resid) is the normalised input."""
+    _check(x, F16, "x")
+    _check(gamma, F32, "gamma")
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    y = out if out is not None else torch.empty_like(x)
+    rstd = torch.empty(rows, device=x.device, dtype=F32)
+    s = x
+    if resid is not None:
+        _check(resid, F16, "resid")
+        s = sum_out if sum_out is not None else torch.empty_like(x)
+    _lib.call("jx_rmsnorm_fwd", x.data_ptr(), _ptr(resid), _ptr(s) if resid is not None else None, gamma.data_ptr(),
+              y.data_ptr(), rstd.data_ptr(), rows, cols, float(eps), _stream())
+    return y, rstd, s
+
+
+def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor, gamma: torch.Tensor,
+                dresid: torch.Tensor | None = None, dgamma: torch.Tensor | None = None, accumulate: bool = False,
+                out: torch.Tensor | None = None, part: torch.Tensor | None = None):
+    """Returns (dx, dgamma); dgamma is accumulated into when `accumulate` and given."""
+    _check(dy, F16, "dy")
+    _check(x, F16, "x")
+    _check(rstd, F32, "rstd")
+    _check(gamma, F32, "gamma")
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    dx = out if out is not None else torch.empty_like(x)
+    nparts = _lib.query("jx_rmsnorm_bwd_parts", rows)
+    if part is None or part.numel() < nparts * cols:
+        part = torch.empty(nparts * cols, device=x.device, dtype=F32)
+    if dresid is not None:
+        _check(dresid, F16, "dresid")
+    _lib.call("jx_rmsnorm_bwd", dy.data_ptr(), x.data_ptr(), rstd.data_ptr(), gamma.data_ptr(), _ptr(dresid),
+              dx.data_ptr(), part.data_ptr(), rows, cols, _stream())
+    if dgamma is None:
+        dgamma = torch.empty(cols, device=x.device, dtype=F32)
+        accumulate = False
+    _lib.call("jx_rmsnorm_dgamma_reduce", part.data_ptr(), nparts, cols, dgamma.data_ptr(), int(accumulate), _stream())
+    return dx, dgamma
+
+
+# ---------------------------------------------------------------- embedding
+def embed_fwd(ids: torch.Tensor, table16: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(ids, I64, "ids")
+    _check(table16, F16, "table16")
+    vocab, cols = table16.shape
+    y = out if out is not None else torch.empty(*ids.shape, cols, device=ids.device, dtype=F16)
+    _lib.call("jx_embed_fwd", ids.data_ptr(), ids.numel(), table16.data_ptr(), vocab, cols, y.data_ptr(), _stream())
+    return y
+
+
+def embed_bwd(ids: torch.Tensor, dout16: torch.Tensor, dtable: torch.Tensor) -> None:
+    _check(ids, I64, "ids")
+    _check(dout16, F16, "dout16")
+    _check(dtable, F32, "dtable")
+    vocab, cols = dtable.shape
+    _lib.call("jx_embed_bwd", ids.data_ptr(), ids.numel(), dout16.data_ptr(), vocab, cols, dtable.data_ptr(),
+              _stream())
+
+
+# ---------------------------------------------------------------- GEMMs
+def _ld(t: torch.Tensor) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError("GEMM operands must be 2-D with unit column stride")
+    return t.stride(0)
+
+
+def gemm_f16(a: torch.Tensor, b: torch.Tensor, a_mn_major: bool = False, b_mn_major: bool = False,
+             resid: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C[m][n] = sum_k A[m][k] B[n][k] (fp16 out). a is [M,K] (or [K,M] if a_mn_major);
+    b is [N,K] (or [K,N] if b_mn_major)."""
+    _check(a, F16, "a", contiguous=False)
+    _check(b, F16, "b", contiguous=False)
+    M, K = (a.shape[1], a.shape[0]) if a_mn_major else a.shape
+    N, Kb = (b.shape[1], b.shape[0]) if b_mn_major else b.shape
+    if K != Kb:
+        raise ValueError(f"inner dimensions differ: {K} vs {Kb}")
+    c = out if out is not None else torch.empty(M, N, device=a.device, dtype=F16)
+    if resid is not None:
+        _check(resid, F16, "resid", contiguous=False)
+    _lib.call("jx_gemm_f16", a.data_ptr(), _ld(a), int(a_mn_major), b.data_ptr(), _ld(b), int(b_mn_major), M, N, K,
+              c.data_ptr(), _ld(c), _ptr(resid), _ld(resid) if resid is not None else 0, _stream())
+    return c
+
+
+def gemm_qkv_rope(x: torch.Tensor, w: torch.Tensor, hidden: int, cos: torch.Tensor, sin: torch.Tensor, seq_len: int,
+                  head_dim: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(x, F16, "x")
+    _check(w, F16, "w")
+    _check(cos, F32, "cos")
+    _check(sin, F32, "sin")
+    M, K = x.shape
+    c = out if out is not None else torch.empty(M, 3 * hidden, device=x.device, dtype=F16)
+    _lib.call("jx_gemm_qkv_rope", x.data_ptr(), K, w.data_ptr(), M, hidden, K, c.data_ptr(), _ld(c), cos.data_ptr(),
+              sin.data_ptr(), seq_len, head_dim, _stream())
+    return c
+
+
+def gemm_swiglu_fwd(x: torch.Tensor, wgu: torch.Tensor, F: int, gate=None, up=None, act=None):
+    _check(x, F16, "x")
+    _check(wgu, F16, "wgu")
+    M, K = x.shape
+    mk = lambda: torch.empty(M, F, device=x.device, dtype=F16)  # noqa: E731
+    gate = gate if gate is not None else mk()
+    up = up if up is not None else mk()
+    act = act if act is not None else mk()
+    _lib.call("jx_gemm_swiglu_fwd", x.data_ptr(), K, wgu.data_ptr(), M, F, K, gate.data_ptr(), up.data_ptr(),
+              act.data_ptr(), F, _stream())
+    return gate, up, act
+
+
+def gemm_swiglu_bwd(dy: torch.Tensor, wd: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """dy [M, d], wd [d, F] -> dgu [M, 2F] = [d gate | d up]."""
+    _check(dy, F16, "dy")
+    _check(wd, F16, "wd")
+    M, K = dy.shape
+    F = wd.shape[1]
+    dgu = out if out is not None else torch.empty(M, 2 * F, device=dy.device, dtype=F16)
+    _lib.call("jx_gemm_swiglu_bwd", dy.data_ptr(), K, wd.data_ptr(), M, F, K, gate.data_ptr(), up.data_ptr(), F,
+              dgu.data_ptr(), _ld(dgu), _stream())
+    return dgu
+
+
+def wgrad_workspace_bytes(N: int, K: int, splits: int) -> int:
+    return _lib.query("jx_gemm_wgrad_workspace_bytes", N, K, splits)
+
+
+def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, g: torch.Tensor, accumulate: bool, splits: int = 1,
+               workspace: torch.Tensor | None = None) -> None:
+    """g[n][k] (+)= f32(f16(sum_t dy[t][n] x[t][k]))."""
+    _check(dy, F16, "dy", contiguous=False)
+    _check(x, F16, "x", contiguous=False)
+    _check(g, F32, "g", contiguous=False)
+    T, N = dy.shape
+    K = x.shape[1]
+    if splits > 1:
+        need = wgrad_workspace_bytes(N, K, splits)
+        if workspace is None or workspace.numel() * workspace.element_size() < need:
+            workspace = torch.empty(need // 4 + 1, device=dy.device, dtype=F32)
+    _lib.call("jx_gemm_wgrad", dy.data_ptr(), _ld(dy), x.data_ptr(), _ld(x), T, N, K, g.data_ptr(), _ld(g),
+              int(accumulate), splits, _ptr(workspace), _stream())
+
+
+# ---------------------------------------------------------------- attention
+def attn_fwd(qkv: torch.Tensor, B: int, T: int, H: int, D: int, out: torch.Tensor | None = None):
+    _check(qkv, F16, "qkv")
+    o = out if out is not None else torch.empty(B * T, H * D, device=qkv.device, dtype=F16)
+    lse = torch.empty(B, H, T, device=qkv.device, dtype=F32)
+    _lib.call("jx_attn_fwd", qkv.data_ptr(), o.data_ptr(), lse.data_ptr(), B, T, H, D, 1.0 / math.sqrt(D), _stream())
+    return o, lse
+
+
+def attn_bwd(qkv, o, do, lse, B, T, H, D, cos=None, sin=None, out=None, delta=None):
+    _check(do, F16, "do")
+    dqkv = out if out is not None else torch.empty_like(qkv)
+    delta = delta if delta is not None else torch.empty(B, H, T, device=qkv.device, dtype=F32)
+    _lib.call("jx_attn_bwd", qkv.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
+              dqkv.data_ptr(), B, T, H, D, 1.0 / math.sqrt(D), _ptr(cos), _ptr(sin), _stream())
+    return dqkv
+
+
+# ---------------------------------------------------------------- cross-entropy
+def ce_fwd(logits16: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100, lse=None, row_loss=None):
+    _check(targets, I64, "targets")
+    rows, vocab = logits16.shape
+    lse = lse if lse is not None else torch.empty(rows, device=logits16.device, dtype=F32)
+    row_loss = row_loss if row_loss is not None else torch.empty(rows, device=logits16.device, dtype=F32)
+    _lib.call("jx_ce_fwd", logits16.data_ptr(), rows, vocab, _ld(logits16), targets.data_ptr(), ignore_index,
+              lse.data_ptr(), row_loss.data_ptr(), _stream())
+    return lse, row_loss
+
+
+def ce_loss(row_loss: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100,
+            out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    out = out if out is not None else torch.zeros(2, device=row_loss.device, dtype=F32)
+    _lib.call("jx_ce_loss", row_loss.data_ptr(), targets.data_ptr(), ignore_index, row_loss.numel(), out.data_ptr(),
+              int(accumulate), _stream())
+    return out
+
+
+def ce_bwd(logits16, targets, lse, grad_loss: torch.Tensor, count: torch.Tensor, ignore_index: int = -100) -> None:
+    rows, vocab = logits16.shape
+    _lib.call("jx_ce_bwd", logits16.data_ptr(), rows, vocab, _ld(logits16), targets.data_ptr(), ignore_index,
+              lse.data_ptr(), grad_loss.data_ptr(), count.data_ptr(), _stream())
+
+
+# ---------------------------------------------------------------- optimizer
+def grad_stats(grad: torch.Tensor, inv_scale: torch.Tensor, partial: torch.Tensor, found_inf: torch.Tensor) -> int:
+    n = grad.numel()
+    nparts = _lib.query("jx_grad_stats_parts", n)
+    _lib.call("jx_grad_stats", grad.data_ptr(), int(grad.dtype == F16), n, inv_scale.data_ptr(), partial.data_ptr(),
+              found_inf.data_ptr(), _stream())
+    return nparts
+
+
+def grad_stats_parts(n: int) -> int:
+    return _lib.query("jx_grad_stats_parts", n)
+
+
+def grad_finalize(partial: torch.Tensor, nparts: int, max_norm: float, out: torch.Tensor) -> None:
+    _lib.call("jx_grad_finalize", partial.data_ptr(), nparts, float(max_norm), out.data_ptr(), _stream())
+
+
+def adamw_step(p, grad, m, v, p16, inv_scale, clip, found_inf, lr, beta1, beta2, eps, wd, step) -> None:
+    _lib.call("jx_adamw_step", p.data_ptr(), grad.data_ptr(), int(grad.dtype == F16), m.data_ptr(), v.data_ptr(),
+              _ptr(p16), p.numel(), _ptr(inv_scale), _ptr(clip), _ptr(found_inf), float(lr), float(beta1),
+              float(beta2), float(eps), float(wd), float(step), _stream())
+
+
+def scaler_update(scale, tracker, found_inf, growth=2.0, backoff=0.5, interval=2000) -> None:
+    _lib.call("jx_scaler_update", scale.data_ptr(), tracker.data_ptr(), found_inf.data_ptr(), float(growth),
+              float(backoff), int(interval), _stream())
+
+
+def cast_f32_f16(src: torch.Tensor, dst: torch.Tensor) -> None:
+    _lib.call("jx_cast_f32_f16", src.data_ptr(), dst.data_ptr(), src.numel(), _stream())
+
+
+def transpose_f16(src: torch.Tensor, dst: torch.Tensor | None = None) -> torch.Tensor:
+    rows, cols = src.shape
+    dst = dst if dst is not None else torch.empty(cols, rows, device=src.device, dtype=F16)
+    _lib.call("jx_transpose_f16", src.data_ptr(), dst.data_ptr(), rows, cols, _stream())
+    return dst

@@ -1,0 +1,271 @@
+"""Per-kernel numerics on the GPU, each against a plain PyTorch fp32 reference
+of the same op on the same fp16 inputs. Tolerance: norm-wise relative error
+2e-3 (fp16 outputs), 1e-2 for attention / cross-entropy gradients."""
+import math
+
+import pytest
+import torch
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+TOL_ATTN = 1e-2
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from midstream_llm_b200 import ops as _ops
+    return _ops
+
+
+def _h(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(*shape, device="cuda", generator=g) * scale).half()
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 128), (296, 264, 200), (1024, 3072, 1024)])
+def test_gemm_f16_majors(ops, a_mn, b_mn, M, N, K):
+    a = _h(M, K, seed=1)
+    b = _h(N, K, seed=2)
+    ref = a.float() @ b.float().t()
+    A = a.t().contiguous() if a_mn else a
+    B = b.t().contiguous() if b_mn else b
+    c = ops.gemm_f16(A, B, a_mn_major=a_mn, b_mn_major=b_mn)
+    torch.cuda.synchronize()
+    assert rel_err(c, ref) < TOL, (a_mn, b_mn, M, N, K, rel_err(c, ref))
+
+
+def test_gemm_resid(ops):
+    M, N, K = 512, 1024, 1024
+    a, b, r = _h(M, K, seed=1), _h(N, K, seed=2), _h(M, N, seed=3)
+    c = ops.gemm_f16(a, b, resid=r)
+    ref = r.float() + (a.float() @ b.float().t()).half().float()
+    assert rel_err(c, ref) < TOL
+
+
+def _rope_tables(T, hd, theta=10000.0):
+    inv = theta ** (-torch.arange(0, hd, 2, device="cuda", dtype=torch.float32) / hd)
+    ang = torch.arange(T, device="cuda", dtype=torch.float32)[:, None] * inv
+    return ang.cos().contiguous(), ang.sin().contiguous()
+
+
+def _rope_ref(x, cos, sin):
+    # x [B, T, H, hd] fp32
+    a, b = x.chunk(2, dim=-1)
+    c, s = cos[None, :, None, :], sin[None, :, None, :]
+    return torch.cat((a * c - b * s, a * s + b * c), dim=-1)
+
+
+def test_gemm_qkv_rope(ops):
+    B, T, H, hd = 2, 256, 4, 64
+    d = H * hd
+    x = _h(B * T, d, seed=4)
+    w = _h(3 * d, d, scale=0.05, seed=5)
+    cos, sin = _rope_tables(T, hd)
+    out = ops.gemm_qkv_rope(x, w, d, cos, sin, T, hd)
+    lin = (x.float() @ w.float().t()).half().float()
+    q, k, v = lin.view(B, T, 3, H, hd).unbind(2)
+    ref = torch.cat([_rope_ref(q, cos, sin).reshape(B * T, d), _rope_ref(k, cos, sin).reshape(B * T, d),
+                     v.reshape(B * T, d)], dim=1)
+    assert rel_err(out, ref) < TOL
+
+
+def test_swiglu_fwd_bwd(ops):
+    M, d, F = 512, 256, 688
+    x = _h(M, d, seed=6)
+    wgu = _h(2 * F, d, scale=0.05, seed=7)
+    wd = _h(d, F, scale=0.05, seed=8)
+    gate, up, act = ops.gemm_swiglu_fwd(x, wgu, F)
+    g_ref = (x.float() @ wgu[:F].float().t())
+    u_ref = (x.float() @ wgu[F:].float().t())
+    assert rel_err(gate, g_ref) < TOL and rel_err(up, u_ref) < TOL
+    act_ref = torch.nn.functional.silu(gate.float()) * up.float()
+    assert rel_err(act, act_ref) < TOL
+    dy = _h(M, d, seed=9)
+    dgu = ops.gemm_swiglu_bwd(dy, wd, gate, up)
+    gf = gate.float().requires_grad_(True)
+    uf = up.float().requires_grad_(True)
+    dact = dy.float() @ wd.float()
+    (torch.nn.functional.silu(gf) * uf).backward(dact)
+    assert rel_err(dgu[:, :F], gf.grad) < TOL
+    assert rel_err(dgu[:, F:], uf.grad) < TOL
+
+
+@pytest.mark.parametrize("splits", [1, 4])
+def test_wgrad(ops, splits):
+    T, N, K = 2048, 1024, 512
+    dy, x = _h(T, N, seed=10), _h(T, K, seed=11)
+    g = torch.randn(N, K, device="cuda")
+    g0 = g.clone()
+    ops.gemm_wgrad(dy, x, g, accumulate=True, splits=splits)
+    ref = g0 + (dy.float().t() @ x.float()).half().float()
+    assert rel_err(g, ref) < TOL
+    ops.gemm_wgrad(dy, x, g, accumulate=False, splits=splits)
+    assert rel_err(g, (dy.float().t() @ x.float())) < TOL
+
+
+@pytest.mark.parametrize("with_resid", [False, True])
+def test_rmsnorm(ops, with_resid):
+    rows, cols = 1000, 1024
+    x = _h(rows, cols, seed=12)
+    r = _h(rows, cols, seed=13) if with_resid else None
+    gamma = (1 + 0.1 * torch.randn(cols, device="cuda")).float()
+    y, rstd, s = ops.rmsnorm_fwd(x, gamma, 1e-5, resid=r)
+    sf = (x.float() + r.float()).half().float() if with_resid else x.float()
+    sf.requires_grad_(True)
+    gf = gamma.clone().requires_grad_(True)
+    yr = torch.nn.functional.rms_norm(sf, (cols,), gf, 1e-5)
+    assert rel_err(y, yr) < TOL
+    if with_resid:
+        assert rel_err(s, sf) < 1e-3
+    dy = _h(rows, cols, seed=14)
+    dres = _h(rows, cols, seed=15) if with_resid else None
+    dx, dg = ops.rmsnorm_bwd(dy, s, rstd, gamma, dresid=dres)
+    yr.backward(dy.float())
+    ref_dx = sf.grad + (dres.float() if with_resid else 0)
+    assert rel_err(dx, ref_dx) < TOL
+    assert rel_err(dg, gf.grad) < TOL
+
+
+def test_embedding(ops):
+    V, d, n = 1000, 256, 4096
+    table = torch.randn(V, d, device="cuda")
+    ids = torch.randint(0, V, (n,), device="cuda")
+    ids[:100] = 7  # a hot row, as Zipf ids produce
+    y = ops.embed_fwd(ids, table.half())
+    assert torch.equal(y, table.half()[ids])
+    dout = _h(n, d, seed=16)
+    dt = torch.zeros(V, d, device="cuda")
+    ops.embed_bwd(ids, dout, dt)
+    ref = torch.zeros(V, d, device="cuda").index_add_(0, ids, dout.float())
+    assert rel_err(dt, ref) < 1e-5
+
+
+def test_cross_entropy(ops):
+    rows, V = 512, 32000
+    logits = _h(rows, V, scale=3.0, seed=17)
+    t = torch.randint(0, V, (rows,), device="cuda")
+    t[5] = -100
+    lse, row_loss = ops.ce_fwd(logits, t)
+    lsc = ops.ce_loss(row_loss, t)
+    lf = logits.float().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(lf, t)
+    torch.cuda.synchronize()
+    loss = lsc[0] / lsc[1]
+    assert abs(float(loss) - float(ref)) / float(ref) < 1e-5
+    gl = torch.tensor([65536.0 / 4], device="cuda")
+    ref.backward(gl[0])
+    d = logits.clone()
+    ops.ce_bwd(d, t, lse, gl, lsc[1:2])
+    assert rel_err(d, lf.grad) < TOL_ATTN
+
+
+def _attn_ref(q, k, v):
+    # q,k,v [B,H,T,D] fp32
+    T = q.shape[2]
+    s = q @ k.transpose(-1, -2) / math.sqrt(q.shape[-1])
+    s = s.masked_fill(torch.ones(T, T, dtype=torch.bool, device=q.device).triu(1), float("-inf"))
+    return s.softmax(-1) @ v
+
+
+@pytest.mark.parametrize("B,T,H", [(2, 256, 4), (1, 1024, 2)])
+def test_attention(ops, B, T, H):
+    D = 64
+    d = H * D
+    qkv = _h(B * T, 3 * d, seed=18)
+    o, lse = ops.attn_fwd(qkv, B, T, H, D)
+    q, k, v = [t.float().view(B, T, H, D).transpose(1, 2).requires_grad_(True)
+               for t in qkv.view(B * T, 3, d).unbind(1)]
+    ref = _attn_ref(q, k, v)
+    assert rel_err(o, ref.transpose(1, 2).reshape(B * T, d)) < TOL
+    do = _h(B * T, d, seed=19)
+    ref.backward(do.float().view(B, T, H, D).transpose(1, 2))
+    dqkv = ops.attn_bwd(qkv, o, do, lse, B, T, H, D)
+    dq, dk, dv = [t.view(B, T, H, D).transpose(1, 2) for t in dqkv.view(B * T, 3, d).unbind(1)]
+    assert rel_err(dv, v.grad) < TOL_ATTN
+    assert rel_err(dk, k.grad) < TOL_ATTN
+    assert rel_err(dq, q.grad) < TOL_ATTN
+
+
+def test_attention_rope_bwd(ops):
+    B, T, H, D = 1, 256, 2, 64
+    d = H * D
+    qkv = _h(B * T, 3 * d, seed=20)
+    cos, sin = _rope_tables(T, D)
+    o, lse = ops.attn_fwd(qkv, B, T, H, D)
+    do = _h(B * T, d, seed=21)
+    plain = ops.attn_bwd(qkv, o, do, lse, B, T, H, D)
+    rot = ops.attn_bwd(qkv, o, do, lse, B, T, H, D, cos=cos, sin=sin)
+    # inverse rotation of the plain q/k gradients
+    for part in range(2):
+        g = plain[:, part * d:(part + 1) * d].float().view(B, T, H, D)
+        g1, g2 = g.chunk(2, dim=-1)
+        c, s = cos[None, :, None, :], sin[None, :, None, :]
+        ref = torch.cat((g1 * c + g2 * s, g2 * c - g1 * s), dim=-1).reshape(B * T, d)
+        assert rel_err(rot[:, part * d:(part + 1) * d], ref) < TOL
+    assert torch.equal(rot[:, 2 * d:], plain[:, 2 * d:])
+
+
+@pytest.mark.parametrize("grad_f16", [False, True])
+def test_adamw_matches_torch(ops, grad_f16):
+    n = 100_003
+    p = torch.randn(n, device="cuda") * 0.02
+    g32 = torch.randn(n, device="cuda") * 1e-3 * 1024
+    g = g32.half() if grad_f16 else g32
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    tp = p.clone().requires_grad_(True)
+    opt = torch.optim.AdamW([tp], lr=3e-4, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1, fused=True)
+    inv = torch.tensor([1 / 1024.0], device="cuda")
+    partial = torch.empty(ops.grad_stats_parts(n), device="cuda")
+    found = torch.zeros(1, device="cuda")
+    nparts = ops.grad_stats(g, inv, partial, found)
+    fin = torch.empty(2, device="cuda")
+    ops.grad_finalize(partial, nparts, 1.0, fin)
+    gu = g.float() * inv
+    total = gu.norm()
+    coef = torch.clamp(1.0 / (total + 1e-6), max=1.0)
+    torch.cuda.synchronize()
+    assert abs(float(fin[0]) - float(total)) / float(total) < 1e-5
+    p16 = torch.empty(n, device="cuda", dtype=torch.float16)
+    for step in (1, 2):
+        ops.adamw_step(p, g, m, v, p16, inv, fin[1:2], found, 3e-4, 0.9, 0.95, 1e-5, 0.1, step)
+        tp.grad = gu * coef
+        opt.step()
+    torch.cuda.synchronize()
+    assert torch.allclose(p, tp.detach(), rtol=1e-6, atol=1e-9)
+    assert torch.equal(p16, p.half())
+
+
+def test_adamw_skips_on_inf(ops):
+    n = 4096
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    g[17] = float("inf")
+    m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    inv = torch.ones(1, device="cuda")
+    partial = torch.empty(ops.grad_stats_parts(n), device="cuda")
+    found = torch.zeros(1, device="cuda")
+    ops.grad_stats(g, inv, partial, found)
+    p0 = p.clone()
+    ops.adamw_step(p, g, m, v, None, inv, None, found, 1e-3, 0.9, 0.95, 1e-5, 0.1, 1)
+    torch.cuda.synchronize()
+    assert float(found) == 1.0
+    assert torch.equal(p, p0) and not m.any()
+
+
+def test_scaler_update(ops):
+    scale = torch.tensor([65536.0], device="cuda")
+    tracker = torch.zeros(1, device="cuda", dtype=torch.int32)
+    found = torch.zeros(1, device="cuda")
+    ops.scaler_update(scale, tracker, found, interval=2)
+    ops.scaler_update(scale, tracker, found, interval=2)
+    torch.cuda.synchronize()
+    assert float(scale) == 131072.0 and int(tracker) == 0
+    found.fill_(1.0)
+    ops.scaler_update(scale, tracker, found, interval=2)
+    torch.cuda.synchronize()
+    assert float(scale) == 65536.0
