@@ -57,7 +57,7 @@ int jx_device_status(int* status_out, int clear);
  * Forward: s = x (+ resid if resid != NULL, stored to sum_out as f16);
  *   rstd[r] = 1/sqrt(mean(s^2) + eps);  y = f16( f16(s*rstd) * gamma ).
  * x, resid, sum_out, y: f16 [rows, cols] contiguous; gamma f32 [cols]; rstd f32 [rows].
- * cols must be a multiple of 8 and <= 8192. */
+ * cols must be a multiple of 8 and <= 4096. */
 int jx_rmsnorm_fwd(const void* x, const void* resid, void* sum_out, const float* gamma, void* y, float* rstd,
                    int64_t rows, int cols, float eps, jx_stream_t stream);
 /* Backward: dx = f16( dresid + f16(d rmsnorm/dx . dy) ) (dresid optional).
@@ -130,8 +130,9 @@ int jx_attn_bwd(const void* qkv, const void* out, const void* dout, const float*
  * target == ignore_index give loss 0 and are excluded from the mean. */
 int jx_ce_fwd(const void* logits16, int64_t rows, int vocab, int64_t ld, const int64_t* targets, int64_t ignore_index,
               float* lse, float* row_loss, jx_stream_t stream);
-/* loss_sum_count[0] = sum of row losses, [1] = number of counted rows
- * (deterministic order); accumulate != 0 adds to the existing values. */
+/* loss_sum_count[0] = sum of row losses, [1] = number of counted rows,
+ * [2] = [0]/[1], the mean loss (deterministic order); accumulate != 0 adds
+ * to the existing sum and count. The buffer holds 3 floats. */
 int jx_ce_loss(const float* row_loss, const int64_t* targets, int64_t ignore_index, int64_t rows,
                float* loss_sum_count, int accumulate, jx_stream_t stream);
 /* In place: logits16 <- f16( (exp(logit - lse) - onehot(target)) * g ),
@@ -152,12 +153,15 @@ int jx_grad_stats(const void* grad, int grad_is_f16, int64_t n, const float* inv
  * out[0] = total_norm, out[1] = clip coefficient. */
 int jx_grad_finalize(const float* partial, int nparts, float max_norm, float* out, jx_stream_t stream);
 /* One decoupled-weight-decay Adam step over flat buffers, skipped entirely
- * (no writes) when *found_inf != 0. Gradient used: (g * inv_scale) * clip.
- * step_count: f32 per-update step number (already incremented) used for the
- * bias corrections. p16 (optional) receives f16(p_new). */
+ * (no writes, step count unchanged) when *found_inf != 0. Gradient used:
+ * (g * inv_scale) * clip (either pointer may be NULL for 1). step_state is a
+ * device f32[4]: [0] holds the number of completed updates and is advanced on
+ * the device before the bias corrections 1-beta^step are formed, as torch's
+ * fused AdamW advances its per-parameter step tensors; [1..3] are scratch.
+ * p16 (optional) receives f16(p_new), the weight copy the GEMMs read. */
 int jx_adamw_step(float* p, const void* grad, int grad_is_f16, float* m, float* v, void* p16, int64_t n,
-                  const float* inv_scale, const float* clip, const float* found_inf, float lr, float beta1,
-                  float beta2, float eps, float weight_decay, float step_count, jx_stream_t stream);
+                  const float* inv_scale, const float* clip, const float* found_inf, float* step_state, float lr,
+                  float beta1, float beta2, float eps, float weight_decay, jx_stream_t stream);
 /* GradScaler.update(): if found_inf: scale *= backoff, tracker = 0; else
  * tracker += 1 and at growth_interval scale *= growth, tracker = 0. */
 int jx_scaler_update(float* scale, int* growth_tracker, const float* found_inf, float growth_factor,

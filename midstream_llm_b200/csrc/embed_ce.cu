@@ -126,8 +126,11 @@ __global__ void ce_loss_kernel(const float* __restrict__ row_loss, const int64_t
     sum = warp_sum(sum);
     cnt = warp_sum(cnt);
     if (lane == 0) {
-      out[0] = accumulate ? out[0] + sum : sum;
-      out[1] = accumulate ? out[1] + cnt : cnt;
+      const float t = accumulate ? out[0] + sum : sum;
+      const float c = accumulate ? out[1] + cnt : cnt;
+      out[0] = t;
+      out[1] = c;
+      out[2] = t / c;
     }
   }
 }

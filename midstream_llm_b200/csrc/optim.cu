@@ -112,15 +112,26 @@ __global__ void grad_finalize_kernel(const float* __restrict__ partial, int npar
 
 struct AdamHyper {
   double lr, beta1, beta2, eps, wd;
-  float bc1, bc2_sqrt;
 };
 
-__device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, const AdamHyper& h) {
+// step_state[0] += 1 unless the update is skipped; [1] = 1 - beta1^step,
+// [2] = sqrt(1 - beta2^step) (double precision, then rounded to fp32).
+__global__ void adamw_prepare_kernel(float* __restrict__ state, const float* __restrict__ found_inf, double beta1,
+                                     double beta2) {
+  if (found_inf && *found_inf != 0.f) return;
+  const float step = state[0] + 1.0f;
+  state[0] = step;
+  state[1] = (float)(1.0 - pow(beta1, (double)step));
+  state[2] = (float)sqrt(1.0 - pow(beta2, (double)step));
+}
+
+__device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, const AdamHyper& h, float bc1,
+                                         float bc2_sqrt) {
   p = (float)((double)p - h.lr * h.wd * (double)p);
   m = (float)(h.beta1 * (double)m + (1.0 - h.beta1) * (double)g);
   v = (float)(h.beta2 * (double)v + (1.0 - h.beta2) * (double)g * (double)g);
-  const float step_size = (float)(h.lr / (double)h.bc1);
-  const float denom = (float)((double)(sqrtf(v) / h.bc2_sqrt) + h.eps);
+  const float step_size = (float)(h.lr / (double)bc1);
+  const float denom = (float)((double)(sqrtf(v) / bc2_sqrt) + h.eps);
   p -= step_size * m / denom;
 }
 
@@ -130,8 +141,10 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(float* __restrict__ p, 
                                                          __half* __restrict__ p16, int64_t n,
                                                          const float* __restrict__ inv_scale,
                                                          const float* __restrict__ clip,
-                                                         const float* __restrict__ found_inf, AdamHyper h) {
+                                                         const float* __restrict__ found_inf,
+                                                         const float* __restrict__ state, AdamHyper h) {
   if (found_inf && *found_inf != 0.f) return;
+  const float bc1 = state[1], bc2s = state[2];
   const float inv = inv_scale ? *inv_scale : 1.0f;
   const float coef = clip ? *clip : 1.0f;
   const int64_t n4 = n / 4;
@@ -146,7 +159,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(float* __restrict__ p, 
     float* ma = &mm.x;
     float* va = &vv.x;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) adam_one(pa[j], (g[j] * inv) * coef, ma[j], va[j], h);
+    for (int j = 0; j < 4; ++j) adam_one(pa[j], (g[j] * inv) * coef, ma[j], va[j], h, bc1, bc2s);
     reinterpret_cast<float4*>(p)[i] = pp;
     reinterpret_cast<float4*>(m)[i] = mm;
     reinterpret_cast<float4*>(v)[i] = vv;
@@ -158,7 +171,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(float* __restrict__ p, 
   }
   for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
     float pv = p[i], mv = m[i], vv = v[i];
-    adam_one(pv, (load_grad1<F16>(grad, i) * inv) * coef, mv, vv, h);
+    adam_one(pv, (load_grad1<F16>(grad, i) * inv) * coef, mv, vv, h, bc1, bc2s);
     p[i] = pv;
     m[i] = mv;
     v[i] = vv;
@@ -251,27 +264,26 @@ extern "C" int jx_grad_finalize(const float* partial, int nparts, float max_norm
 }
 
 extern "C" int jx_adamw_step(float* p, const void* grad, int grad_is_f16, float* m, float* v, void* p16, int64_t n,
-                             const float* inv_scale, const float* clip, const float* found_inf, float lr, float beta1,
-                             float beta2, float eps, float weight_decay, float step_count, jx_stream_t stream) {
-  JX_CHECK_ARG(p && grad && m && v && n > 0, "jx_adamw_step: bad argument");
+                             const float* inv_scale, const float* clip, const float* found_inf, float* step_state,
+                             float lr, float beta1, float beta2, float eps, float weight_decay, jx_stream_t stream) {
+  JX_CHECK_ARG(p && grad && m && v && step_state && n > 0, "jx_adamw_step: bad argument");
   JX_CHECK_ARG(aligned16(p) && aligned16(grad) && aligned16(m) && aligned16(v) && (!p16 || ((uintptr_t)p16 & 7) == 0),
                "jx_adamw_step: buffers must be 16-byte aligned (p16 8-byte)");
-  JX_CHECK_ARG(step_count >= 1.f, "jx_adamw_step: step_count must be >= 1");
   AdamHyper h;
   h.lr = lr;
   h.beta1 = beta1;
   h.beta2 = beta2;
   h.eps = eps;
   h.wd = weight_decay;
-  h.bc1 = (float)(1.0 - pow((double)beta1, (double)step_count));
-  h.bc2_sqrt = (float)sqrt(1.0 - pow((double)beta2, (double)step_count));
-  const int grid = blocks_for(n);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  adamw_prepare_kernel<<<1, 1, 0, s>>>(step_state, found_inf, (double)beta1, (double)beta2);
+  JX_CHECK_LAUNCH("jx_adamw_step: prepare");
+  const int grid = blocks_for(n);
   __half* ph = static_cast<__half*>(p16);
   if (grad_is_f16)
-    adamw_kernel<true><<<grid, kThreads, 0, s>>>(p, grad, m, v, ph, n, inv_scale, clip, found_inf, h);
+    adamw_kernel<true><<<grid, kThreads, 0, s>>>(p, grad, m, v, ph, n, inv_scale, clip, found_inf, step_state, h);
   else
-    adamw_kernel<false><<<grid, kThreads, 0, s>>>(p, grad, m, v, ph, n, inv_scale, clip, found_inf, h);
+    adamw_kernel<false><<<grid, kThreads, 0, s>>>(p, grad, m, v, ph, n, inv_scale, clip, found_inf, step_state, h);
   JX_CHECK_LAUNCH("jx_adamw_step");
   return JX_OK;
 }

@@ -1,0 +1,201 @@
+"""Data-parallel runtime: launch environment, runtime plan, and the bucketed
+gradient all-reduce that overlaps the decoder's backward.
+
+Launch / plan semantics follow Midstream-LLM src/jishui/distributed.py:35-67
+(`LaunchEnvironment.from_environ`: RANK/LOCAL_RANK/WORLD_SIZE all or
+nothing), :302-349 (`build_runtime_plan`: cuda -> nccl on cuda:LOCAL_RANK,
+cpu -> gloo, one accelerator type per job) and :371-409
+(`initialize_runtime`: bind the device, init the process group from env://).
+The reference has no gradient exchange; the rules it documents for one
+(docs/torch-distributed.md:62-67: rank-seeded samplers, no all-reduce on
+non-final accumulation micro-steps, rank-0 checkpoints then a barrier) are
+what `GradReducer` and the trainer implement.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import asdict, dataclass
+from typing import Mapping
+
+import torch
+import torch.distributed as dist
+
+
+class DistributedCapabilityError(RuntimeError):
+    """Raised when a requested topology cannot be supported."""
+
+
+@dataclass(frozen=True)
+class LaunchEnvironment:
+    rank: int = 0
+    local_rank: int = 0
+    world_size: int = 1
+
+    @classmethod
+    def from_environ(cls, environ: Mapping[str, str] | None = None) -> "LaunchEnvironment":
+        values = os.environ if environ is None else environ
+        keys = ("RANK", "LOCAL_RANK", "WORLD_SIZE")
+        present = [k in values for k in keys]
+        if any(present) and not all(present):
+            missing = ", ".join(k for k, ok in zip(keys, present) if not ok)
+            raise DistributedCapabilityError("incomplete torchrun environment; missing " + missing)
+        if not any(present):
+            return cls()
+        try:
+            env = cls(rank=int(values["RANK"]), local_rank=int(values["LOCAL_RANK"]),
+                      world_size=int(values["WORLD_SIZE"]))
+        except ValueError as exc:
+            raise DistributedCapabilityError("RANK, LOCAL_RANK, and WORLD_SIZE must be integers") from exc
+        if env.world_size < 1:
+            raise DistributedCapabilityError("WORLD_SIZE must be positive")
+        if not 0 <= env.rank < env.world_size:
+            raise DistributedCapabilityError(f"RANK={env.rank} must be in [0, WORLD_SIZE={env.world_size})")
+        if env.local_rank < 0:
+            raise DistributedCapabilityError("LOCAL_RANK must be non-negative")
+        return env
+
+
+@dataclass(frozen=True)
+class RuntimePlan:
+    accelerator: str
+    device: str
+    process_group_backend: str | None
+    rank: int
+    local_rank: int
+    world_size: int
+
+    @property
+    def distributed(self) -> bool:
+        return self.world_size > 1
+
+    def to_dict(self) -> dict:
+        d = asdict(self)
+        d["distributed"] = self.distributed
+        return d
+
+
+def build_runtime_plan(accelerators, launch: LaunchEnvironment | None = None) -> RuntimePlan:
+    """cuda -> NCCL on cuda:LOCAL_RANK; cpu -> gloo. Mixed accelerators are rejected."""
+    launch = launch or LaunchEnvironment()
+    requested = (accelerators,) if isinstance(accelerators, str) else tuple(accelerators)
+    requested = tuple(dict.fromkeys(a.strip().lower() for a in requested))
+    if requested == ("auto",):
+        requested = ("cuda" if torch.cuda.is_available() else "cpu",)
+    if len(requested) != 1:
+        raise DistributedCapabilityError(
+            f"one DDP process group cannot mix accelerator types ({', '.join(requested)}); use a homogeneous job")
+    acc = requested[0]
+    if acc not in {"cuda", "cpu"}:
+        raise DistributedCapabilityError(f"accelerator {acc!r} is not supported by the B200 build (cuda or cpu)")
+    return RuntimePlan(accelerator=acc, device=f"cuda:{launch.local_rank}" if acc == "cuda" else "cpu",
+                       process_group_backend="nccl" if acc == "cuda" else "gloo", rank=launch.rank,
+                       local_rank=launch.local_rank, world_size=launch.world_size)
+
+
+@dataclass
+class RuntimeContext:
+    plan: RuntimePlan
+    torch_device: torch.device
+    created_process_group: bool
+
+    def close(self) -> None:
+        if self.created_process_group and dist.is_initialized():
+            dist.destroy_process_group()
+        self.created_process_group = False
+
+    def __enter__(self) -> "RuntimeContext":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+
+def initialize_runtime(plan: RuntimePlan, timeout_s: float | None = None) -> RuntimeContext:
+    """Binds the local device and (for world_size > 1) creates the process group."""
+    if plan.accelerator == "cuda":
+        if not torch.cuda.is_available():
+            raise DistributedCapabilityError("cuda runtime is unavailable")
+        if plan.local_rank >= torch.cuda.device_count():
+            raise DistributedCapabilityError(
+                f"LOCAL_RANK={plan.local_rank} exceeds the {torch.cuda.device_count()} visible cuda device(s)")
+        torch.cuda.set_device(plan.local_rank)
+    created = False
+    if plan.distributed:
+        if dist.is_initialized():
+            raise DistributedCapabilityError("a torch process group is already initialized")
+        kwargs = {}
+        if timeout_s is not None:
+            import datetime
+            kwargs["timeout"] = datetime.timedelta(seconds=timeout_s)
+        if plan.accelerator == "cuda":
+            kwargs["device_id"] = torch.device(plan.device)
+        dist.init_process_group(backend=plan.process_group_backend, init_method="env://", rank=plan.rank,
+                                world_size=plan.world_size, **kwargs)
+        created = True
+    return RuntimeContext(plan=plan, torch_device=torch.device(plan.device), created_process_group=created)
+
+
+class GradReducer:
+    """Averages the flat fp32 gradient buffer across ranks while backward runs.
+
+    The decoder's backward calls `ready(lo, hi)` each time a contiguous range
+    of the flat gradient buffer is final (the final norm, then each layer from
+    the last to the first, then the tied embedding). Ranges are merged into
+    buckets of about `bucket_bytes` and each bucket is all-reduced (AVG)
+    asynchronously on NCCL's stream as soon as it fills, so communication of
+    layer l overlaps the backward of layers l-1..0. `finish()` makes the
+    compute stream wait for every outstanding bucket. Set `enabled = False`
+    for non-final gradient-accumulation micro-steps.
+    """
+
+    def __init__(self, group=None, bucket_bytes: int = 25 * 1024 * 1024):
+        self.group = group
+        self.bucket_elems = max(1, bucket_bytes // 4)
+        self.enabled = True
+        self._works: list = []
+        self._lo = self._hi = None
+        self._flat = None
+        self.launched: list[tuple[int, int]] = []
+
+    def world_size(self) -> int:
+        return dist.get_world_size(self.group) if dist.is_initialized() else 1
+
+    def begin(self, flat) -> None:
+        self._flat = flat
+        self._works.clear()
+        self._lo = self._hi = None
+        self.launched = []
+
+    def _launch(self, lo: int, hi: int) -> None:
+        view = self._flat.g32[lo:hi]
+        op = dist.ReduceOp.AVG if dist.get_backend(self.group) == "nccl" else dist.ReduceOp.SUM
+        work = dist.all_reduce(view, op=op, group=self.group, async_op=True)
+        self._works.append((work, view, op))
+        self.launched.append((lo, hi))
+
+    def ready(self, lo: int, hi: int) -> None:
+        if not self.enabled or self.world_size() == 1:
+            return
+        if self._lo is None:
+            self._lo, self._hi = lo, hi
+        elif hi == self._lo:
+            self._lo = lo
+        else:  # not adjacent: flush what we have and start a new span
+            self._launch(self._lo, self._hi)
+            self._lo, self._hi = lo, hi
+        while self._hi - self._lo >= self.bucket_elems:
+            self._launch(self._hi - self.bucket_elems, self._hi)
+            self._hi -= self.bucket_elems
+
+    def finish(self) -> None:
+        if not self.enabled or self.world_size() == 1:
+            return
+        if self._lo is not None and self._hi > self._lo:
+            self._launch(self._lo, self._hi)
+        self._lo = self._hi = None
+        ws = self.world_size()
+        for work, view, op in self._works:
+            work.wait()
+            if op == dist.ReduceOp.SUM:
+                view.div_(ws)
+        self._works.clear()

@@ -37,14 +37,15 @@ def _check(t: torch.Tensor, dtype: torch.dtype, name: str, contiguous: bool = Tr
 
 # ---------------------------------------------------------------- RMSNorm
 def rmsnorm_fwd(x: torch.Tensor, gamma: torch.Tensor, eps: float, resid: torch.Tensor | None = None,
-                out: torch.Tensor | None = None, sum_out: torch.Tensor | None = None):
+                out: torch.Tensor | None = None, sum_out: torch.Tensor | None = None,
+                rstd: torch.Tensor | None = None):
     """Returns (y, rstd, s) where s = x (+ resid) is the normalised input."""
     _check(x, F16, "x")
     _check(gamma, F32, "gamma")
     cols = x.shape[-1]
     rows = x.numel() // cols
     y = out if out is not None else torch.empty_like(x)
-    rstd = torch.empty(rows, device=x.device, dtype=F32)
+    rstd = rstd if rstd is not None else torch.empty(rows, device=x.device, dtype=F32)
     s = x
     if resid is not None:
         _check(resid, F16, "resid")
@@ -183,10 +184,11 @@ def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, g: torch.Tensor, accumulate: b
 
 
 # ---------------------------------------------------------------- attention
-def attn_fwd(qkv: torch.Tensor, B: int, T: int, H: int, D: int, out: torch.Tensor | None = None):
+def attn_fwd(qkv: torch.Tensor, B: int, T: int, H: int, D: int, out: torch.Tensor | None = None,
+             lse: torch.Tensor | None = None):
     _check(qkv, F16, "qkv")
     o = out if out is not None else torch.empty(B * T, H * D, device=qkv.device, dtype=F16)
-    lse = torch.empty(B, H, T, device=qkv.device, dtype=F32)
+    lse = lse if lse is not None else torch.empty(B, H, T, device=qkv.device, dtype=F32)
     _lib.call("jx_attn_fwd", qkv.data_ptr(), o.data_ptr(), lse.data_ptr(), B, T, H, D, 1.0 / math.sqrt(D), _stream())
     return o, lse
 
@@ -213,7 +215,7 @@ def ce_fwd(logits16: torch.Tensor, targets: torch.Tensor, ignore_index: int = -1
 
 def ce_loss(row_loss: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100,
             out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
-    out = out if out is not None else torch.zeros(2, device=row_loss.device, dtype=F32)
+    out = out if out is not None else torch.zeros(3, device=row_loss.device, dtype=F32)
     _lib.call("jx_ce_loss", row_loss.data_ptr(), targets.data_ptr(), ignore_index, row_loss.numel(), out.data_ptr(),
               int(accumulate), _stream())
     return out
@@ -242,10 +244,12 @@ def grad_finalize(partial: torch.Tensor, nparts: int, max_norm: float, out: torc
     _lib.call("jx_grad_finalize", partial.data_ptr(), nparts, float(max_norm), out.data_ptr(), _stream())
 
 
-def adamw_step(p, grad, m, v, p16, inv_scale, clip, found_inf, lr, beta1, beta2, eps, wd, step) -> None:
+def adamw_step(p, grad, m, v, p16, inv_scale, clip, found_inf, step_state, lr, beta1, beta2, eps, wd) -> None:
+    """step_state: f32[4] device tensor; [0] is the completed-update count, advanced on
+    the device unless *found_inf != 0."""
     _lib.call("jx_adamw_step", p.data_ptr(), grad.data_ptr(), int(grad.dtype == F16), m.data_ptr(), v.data_ptr(),
-              _ptr(p16), p.numel(), _ptr(inv_scale), _ptr(clip), _ptr(found_inf), float(lr), float(beta1),
-              float(beta2), float(eps), float(wd), float(step), _stream())
+              _ptr(p16), p.numel(), _ptr(inv_scale), _ptr(clip), _ptr(found_inf), step_state.data_ptr(), float(lr),
+              float(beta1), float(beta2), float(eps), float(wd), _stream())
 
 
 def scaler_update(scale, tracker, found_inf, growth=2.0, backoff=0.5, interval=2000) -> None:

@@ -1,0 +1,3 @@
+"""ORACLE — test infrastructure: a CPU/PyTorch restatement of the reference's
+training step, the checker for the B200 kernels. Only tests/, bench.py's
+CPU-baseline and reference legs, and __graft_entry__.smoke() may import it."""

@@ -231,13 +231,15 @@ def test_adamw_matches_torch(ops, grad_f16):
     torch.cuda.synchronize()
     assert abs(float(fin[0]) - float(total)) / float(total) < 1e-5
     p16 = torch.empty(n, device="cuda", dtype=torch.float16)
+    state = torch.zeros(4, device="cuda")
     for step in (1, 2):
-        ops.adamw_step(p, g, m, v, p16, inv, fin[1:2], found, 3e-4, 0.9, 0.95, 1e-5, 0.1, step)
+        ops.adamw_step(p, g, m, v, p16, inv, fin[1:2], found, state, 3e-4, 0.9, 0.95, 1e-5, 0.1)
         tp.grad = gu * coef
         opt.step()
     torch.cuda.synchronize()
     assert torch.allclose(p, tp.detach(), rtol=1e-6, atol=1e-9)
     assert torch.equal(p16, p.half())
+    assert float(state[0]) == 2.0
 
 
 def test_adamw_skips_on_inf(ops):
@@ -251,10 +253,12 @@ def test_adamw_skips_on_inf(ops):
     found = torch.zeros(1, device="cuda")
     ops.grad_stats(g, inv, partial, found)
     p0 = p.clone()
-    ops.adamw_step(p, g, m, v, None, inv, None, found, 1e-3, 0.9, 0.95, 1e-5, 0.1, 1)
+    state = torch.zeros(4, device="cuda")
+    ops.adamw_step(p, g, m, v, None, inv, None, found, state, 1e-3, 0.9, 0.95, 1e-5, 0.1)
     torch.cuda.synchronize()
     assert float(found) == 1.0
     assert torch.equal(p, p0) and not m.any()
+    assert float(state[0]) == 0.0
 
 
 def test_scaler_update(ops):
