@@ -48,6 +48,8 @@ typedef struct CUstream_st* jx_stream_t; /* == cudaStream_t */
 int jx_version(void);
 /* Text of the last error on this host thread ("" if none). */
 const char* jx_last_error(void);
+/* Number of kernels this library has launched in this process. */
+int64_t jx_launch_count(void);
 /* Device-side status word: non-zero when a kernel abandoned work after a
  * bounded wait expired (code identifies the wait). Reads and optionally clears
  * it; synchronises the current device. */

@@ -16,6 +16,7 @@ _P = c_void_p
 _SIGNATURES: dict[str, tuple] = {
     "jx_version": (c_int, []),
     "jx_last_error": (ctypes.c_char_p, []),
+    "jx_launch_count": (c_int64, []),
     "jx_device_status": (c_int, [ctypes.POINTER(c_int), c_int]),
     "jx_rmsnorm_fwd": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, c_int, c_float, _P]),
     "jx_rmsnorm_bwd_parts": (c_int, [c_int64]),
@@ -83,6 +84,11 @@ def call(name: str, *args) -> None:
 
 def query(name: str, *args):
     return getattr(load(), name)(*args)
+
+
+def launch_count() -> int:
+    """Kernels launched by libjishui_b200.so so far in this process."""
+    return int(load().jx_launch_count())
 
 
 def device_status(clear: bool = True) -> int:

@@ -3,6 +3,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "jx_common.cuh"
@@ -11,6 +12,9 @@
 namespace jx {
 
 static thread_local char g_last_error[512] = "";
+static std::atomic<long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -56,6 +60,8 @@ int num_sms() {
 extern "C" int jx_version(void) { return 100; }
 
 extern "C" const char* jx_last_error(void) { return jx::g_last_error; }
+
+extern "C" int64_t jx_launch_count(void) { return jx::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int jx_device_status(int* status_out, int clear) {
   JX_CHECK_ARG(status_out != nullptr, "jx_device_status: status_out is NULL");

@@ -17,6 +17,8 @@ namespace jx {
 // last failure on the calling host thread is kept for jx_last_error().
 // ---------------------------------------------------------------------------
 void set_error(const char* fmt, ...);
+// Counts successful kernel launches (exported as jx_launch_count()).
+void count_launch();
 
 #define JX_CHECK_ARG(cond, ...)              \
   do {                                       \
@@ -33,6 +35,7 @@ void set_error(const char* fmt, ...);
       ::jx::set_error("%s: launch failed: %s", what, cudaGetErrorString(_e));   \
       return JX_ERR_LAUNCH;                                                     \
     }                                                                           \
+    ::jx::count_launch();                                                       \
   } while (0)
 
 #define JX_CUDA_TRY(call, what)                                                  \

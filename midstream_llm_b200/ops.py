@@ -15,6 +15,35 @@ from . import _lib
 
 F16, F32, I64 = torch.float16, torch.float32, torch.int64
 
+# When set to a list, every GEMM launch appends (algorithmic FLOPs, start event,
+# end event) recorded on the launching stream (used by bench.py's roofline).
+_GEMM_PROFILE: list | None = None
+
+
+def set_gemm_profile(records: list | None) -> None:
+    global _GEMM_PROFILE
+    _GEMM_PROFILE = records
+
+
+class _GemmTimer:
+    __slots__ = ("flops", "start")
+
+    def __init__(self, flops: float):
+        self.flops = flops
+        self.start = None
+
+    def __enter__(self):
+        if _GEMM_PROFILE is not None:
+            self.start = torch.cuda.Event(enable_timing=True)
+            self.start.record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.start is not None and _GEMM_PROFILE is not None:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            _GEMM_PROFILE.append((self.flops, self.start, end))
+
 
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
@@ -119,8 +148,9 @@ def gemm_f16(a: torch.Tensor, b: torch.Tensor, a_mn_major: bool = False, b_mn_ma
     c = out if out is not None else torch.empty(M, N, device=a.device, dtype=F16)
     if resid is not None:
         _check(resid, F16, "resid", contiguous=False)
-    _lib.call("jx_gemm_f16", a.data_ptr(), _ld(a), int(a_mn_major), b.data_ptr(), _ld(b), int(b_mn_major), M, N, K,
-              c.data_ptr(), _ld(c), _ptr(resid), _ld(resid) if resid is not None else 0, _stream())
+    with _GemmTimer(2.0 * M * N * K):
+        _lib.call("jx_gemm_f16", a.data_ptr(), _ld(a), int(a_mn_major), b.data_ptr(), _ld(b), int(b_mn_major), M, N,
+                  K, c.data_ptr(), _ld(c), _ptr(resid), _ld(resid) if resid is not None else 0, _stream())
     return c
 
 
@@ -132,8 +162,9 @@ def gemm_qkv_rope(x: torch.Tensor, w: torch.Tensor, hidden: int, cos: torch.Tens
     _check(sin, F32, "sin")
     M, K = x.shape
     c = out if out is not None else torch.empty(M, 3 * hidden, device=x.device, dtype=F16)
-    _lib.call("jx_gemm_qkv_rope", x.data_ptr(), K, w.data_ptr(), M, hidden, K, c.data_ptr(), _ld(c), cos.data_ptr(),
-              sin.data_ptr(), seq_len, head_dim, _stream())
+    with _GemmTimer(2.0 * M * 3 * hidden * K):
+        _lib.call("jx_gemm_qkv_rope", x.data_ptr(), K, w.data_ptr(), M, hidden, K, c.data_ptr(), _ld(c),
+                  cos.data_ptr(), sin.data_ptr(), seq_len, head_dim, _stream())
     return c
 
 
@@ -145,8 +176,9 @@ def gemm_swiglu_fwd(x: torch.Tensor, wgu: torch.Tensor, F: int, gate=None, up=No
     gate = gate if gate is not None else mk()
     up = up if up is not None else mk()
     act = act if act is not None else mk()
-    _lib.call("jx_gemm_swiglu_fwd", x.data_ptr(), K, wgu.data_ptr(), M, F, K, gate.data_ptr(), up.data_ptr(),
-              act.data_ptr(), F, _stream())
+    with _GemmTimer(2.0 * M * 2 * F * K):
+        _lib.call("jx_gemm_swiglu_fwd", x.data_ptr(), K, wgu.data_ptr(), M, F, K, gate.data_ptr(), up.data_ptr(),
+                  act.data_ptr(), F, _stream())
     return gate, up, act
 
 
@@ -158,8 +190,9 @@ def gemm_swiglu_bwd(dy: torch.Tensor, wd: torch.Tensor, gate: torch.Tensor, up: 
     M, K = dy.shape
     F = wd.shape[1]
     dgu = out if out is not None else torch.empty(M, 2 * F, device=dy.device, dtype=F16)
-    _lib.call("jx_gemm_swiglu_bwd", dy.data_ptr(), K, wd.data_ptr(), M, F, K, gate.data_ptr(), up.data_ptr(), F,
-              dgu.data_ptr(), _ld(dgu), _stream())
+    with _GemmTimer(2.0 * M * F * K):
+        _lib.call("jx_gemm_swiglu_bwd", dy.data_ptr(), K, wd.data_ptr(), M, F, K, gate.data_ptr(), up.data_ptr(), F,
+                  dgu.data_ptr(), _ld(dgu), _stream())
     return dgu
 
 
@@ -179,8 +212,9 @@ def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, g: torch.Tensor, accumulate: b
         need = wgrad_workspace_bytes(N, K, splits)
         if workspace is None or workspace.numel() * workspace.element_size() < need:
             workspace = torch.empty(need // 4 + 1, device=dy.device, dtype=F32)
-    _lib.call("jx_gemm_wgrad", dy.data_ptr(), _ld(dy), x.data_ptr(), _ld(x), T, N, K, g.data_ptr(), _ld(g),
-              int(accumulate), splits, _ptr(workspace), _stream())
+    with _GemmTimer(2.0 * T * N * K):
+        _lib.call("jx_gemm_wgrad", dy.data_ptr(), _ld(dy), x.data_ptr(), _ld(x), T, N, K, g.data_ptr(), _ld(g),
+                  int(accumulate), splits, _ptr(workspace), _stream())
 
 
 # ---------------------------------------------------------------- attention
