@@ -235,22 +235,36 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(const __half* __restrict_
   }
 }
 
-// delta[b,h,t] = sum_c dO[t, h*64+c] * O[t, h*64+c]
+// delta[b,h,t] = sum_c dO[t, h*64+c] * O[t, h*64+c]; eight threads per
+// (token, head), 16-byte loads.
 __global__ void attn_delta_kernel(const __half* __restrict__ out, const __half* __restrict__ dout,
                                   float* __restrict__ delta, int B, int T, int H) {
-  const int lane = threadIdx.x & 31;
-  const int64_t w = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t item = gid >> 3;  // (token, head)
+  const int sub = threadIdx.x & 7;
   const int64_t total = (int64_t)B * T * H;
-  if (w >= total) return;
-  const int h = (int)(w % H);
-  const int64_t tok = w / H;
-  const int d = H * D;
-  const __half2 a = *reinterpret_cast<const __half2*>(out + tok * d + h * D + lane * 2);
-  const __half2 g = *reinterpret_cast<const __half2*>(dout + tok * d + h * D + lane * 2);
-  const float2 af = __half22float2(a), gf = __half22float2(g);
-  float s = af.x * gf.x + af.y * gf.y;
-  s = warp_sum(s);
-  if (lane == 0) {
+  float s = 0.f;
+  if (item < total) {
+    const int h = (int)(item % H);
+    const int64_t tok = item / H;
+    const int d = H * D;
+    const int64_t off = tok * d + h * D + sub * 8;
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(out + off));
+    const uint4 g = __ldg(reinterpret_cast<const uint4*>(dout + off));
+    const __half2* ah = reinterpret_cast<const __half2*>(&a);
+    const __half2* gh = reinterpret_cast<const __half2*>(&g);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 af = __half22float2(ah[j]), gf = __half22float2(gh[j]);
+      s += af.x * gf.x + af.y * gf.y;
+    }
+  }
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  s += __shfl_xor_sync(0xffffffffu, s, 4);
+  if (item < total && sub == 0) {
+    const int h = (int)(item % H);
+    const int64_t tok = item / H;
     const int b = (int)(tok / T), t = (int)(tok % T);
     delta[((int64_t)b * H + h) * T + t] = s;
   }
@@ -516,8 +530,8 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
                "jx_attn_bwd: buffers must be 16-byte aligned");
   JX_CHECK_ARG((rope_cos == nullptr) == (rope_sin == nullptr), "jx_attn_bwd: pass both RoPE tables or neither");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t warps = (int64_t)B * T * H;
-  attn_delta_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(static_cast<const __half*>(out),
+  const int64_t threads = (int64_t)B * T * H * 8;
+  attn_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(static_cast<const __half*>(out),
                                                                 static_cast<const __half*>(dout), delta, B, T, H);
   JX_CHECK_LAUNCH("jx_attn_bwd: delta");
   const float scale_log2 = scale * 1.4426950408889634f;

@@ -60,11 +60,12 @@ __global__ void ce_fwd_kernel(const __half* __restrict__ logits, int64_t rows, i
   float m = -INFINITY, s = 0.f;
   const int nvec = vocab / 8;
   for (int i = lane; i < nvec; i += 32) {
-    half8 h = *reinterpret_cast<const half8*>(x + i * 8);
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + i * 8);
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
     float v[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float2 f = __half22float2(h.h[j]);
+      float2 f = __half22float2(h[j]);
       v[2 * j] = f.x;
       v[2 * j + 1] = f.y;
     }
@@ -148,16 +149,17 @@ __global__ void ce_bwd_kernel(__half* __restrict__ logits, int64_t rows, int voc
   const float l = lse[row];
   const int nvec = vocab / 8;
   for (int i = lane; i < nvec; i += 32) {
-    half8 h = *reinterpret_cast<const half8*>(x + i * 8);
+    uint4 raw = *reinterpret_cast<const uint4*>(x + i * 8);
+    __half2* h = reinterpret_cast<__half2*>(&raw);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float2 f = __half22float2(h.h[j]);
+      float2 f = __half22float2(h[j]);
       const int c0 = i * 8 + 2 * j;
       float a = expf(f.x - l) - (c0 == t ? 1.f : 0.f);
       float b = expf(f.y - l) - (c0 + 1 == t ? 1.f : 0.f);
-      h.h[j] = __floats2half2_rn(a * g, b * g);
+      h[j] = __floats2half2_rn(a * g, b * g);
     }
-    *reinterpret_cast<half8*>(x + i * 8) = h;
+    *reinterpret_cast<uint4*>(x + i * 8) = raw;
   }
   for (int c = nvec * 8 + lane; c < vocab; c += 32) {
     const float v = __half2float(x[c]);

@@ -2,10 +2,11 @@
 //
 // acc[m][n] = sum_k A[m][k] * B[n][k]; fp16 operands staged by TMA into
 // 128B-swizzled shared memory, fp32 accumulators in tensor memory (TMEM).
-// One CTA per SM (persistent), 192 threads:
+// One CTA per SM (persistent), 320 threads:
 //   warp 0      TMA producer (one elected lane) filling a 4-stage ring,
 //   warp 1      TMEM allocator + MMA issuer (one elected lane),
-//   warps 2..5  epilogue: tcgen05.ld from TMEM -> fused math -> global stores.
+//   warps 2..9  epilogue: tcgen05.ld from TMEM -> fused math -> global stores
+//               (two warps per TMEM lane quarter, each on half of the columns).
 // The accumulator is double-buffered in TMEM (2 x 256 columns) so the
 // epilogue of tile i overlaps the main loop of tile i+1.
 //
@@ -35,7 +36,8 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
 constexpr int STAGES = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer warp + MMA warp + epilogue warps
 constexpr uint32_t kABytes = BM * BK * 2;  // 16 KiB
 constexpr uint32_t kBBytes = BN * BK * 2;  // 32 KiB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -102,6 +104,31 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& mb, int
 
 __device__ __forceinline__ float h2f_round(float x) { return __half2float(__float2half_rn(x)); }
 
+// Raw 16-byte loads of 32 consecutive fp16 values of one row (zero outside [M, N)).
+__device__ __forceinline__ void load_raw32(const __half* base, int64_t ld, int row, int col, int M, int N,
+                                           uint4 (&r)[4]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (row < M && col + g * 8 + 8 <= N)
+      r[g] = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)row * ld + col + g * 8));
+    else
+      r[g] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ void unpack32(const uint4 (&r)[4], float (&v)[32]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const __half2* h = reinterpret_cast<const __half2*>(&r[g]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __half22float2(h[j]);
+      v[g * 8 + 2 * j] = f.x;
+      v[g * 8 + 2 * j + 1] = f.y;
+    }
+  }
+}
+
 // Store 32 consecutive fp32 values of row `row` starting at column `col` as fp16.
 __device__ __forceinline__ void store_row32_f16(__half* base, int64_t ld, int row, int col, int M, int N,
                                                 const float (&v)[32]) {
@@ -110,82 +137,130 @@ __device__ __forceinline__ void store_row32_f16(__half* base, int64_t ld, int ro
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     if (col + g * 8 + 8 <= N) {
-      half8 h;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) h.h[j] = __floats2half2_rn(v[g * 8 + 2 * j], v[g * 8 + 2 * j + 1]);
-      *reinterpret_cast<half8*>(dst + g * 8) = h;
-    }
-  }
-}
-
-__device__ __forceinline__ void load_row32_f16(const __half* base, int64_t ld, int row, int col, int M, int N,
-                                               float (&v)[32]) {
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    if (row < M && col + g * 8 + 8 <= N) {
-      half8 h = *reinterpret_cast<const half8*>(base + (int64_t)row * ld + col + g * 8);
+      uint32_t w[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float2 f = __half22float2(h.h[j]);
-        v[g * 8 + 2 * j] = f.x;
-        v[g * 8 + 2 * j + 1] = f.y;
+        __half2 h = __floats2half2_rn(v[g * 8 + 2 * j], v[g * 8 + 2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[g * 8 + j] = 0.f;
+      *reinterpret_cast<uint4*>(dst + g * 8) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
 
-__device__ __forceinline__ void tmem_load32f(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  tmem_ld32(taddr, r);
-  tmem_ld_wait();
+__device__ __forceinline__ void to_f32(const uint32_t (&r)[32], float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, 1.0f + expf(-x)); }
+// silu(x) = x / (1 + e^-x), sigmoid(x) = 1 / (1 + e^-x) with the fast exp and
+// division; the results are rounded to fp16, where the difference to the
+// correctly rounded fp32 forms is below half an fp16 ulp except at rounding ties.
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
+// Epilogue of one 128 x 256 accumulator tile. Eight warps drain it: warp
+// quarter q (= warp % 4) owns TMEM lanes / tile rows [32q, 32q+32), and half
+// h owns half of the columns (for kSwigluF: half of the gate and of the up
+// columns; for kRope: two of the four heads). Each thread owns one row.
 template <int EPI>
-__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, int quarter, int lane, int mb, int nb,
-                                              int split) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, int quarter, int half, int lane, int mb,
+                                              int nb, int split) {
   const int row = mb * BM + quarter * 32 + lane;
   const uint32_t tl = tacc + (static_cast<uint32_t>(quarter * 32) << 16);
-  if constexpr (EPI == kF16) {
+  if constexpr (EPI == kF16 || EPI == kWgrad) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int col = nb * BN + c * 32;
-      if (col >= p.N) break;
-      float v[32];
-      tmem_load32f(tl + c * 32, v);
-      if (p.resid) {
-        float r[32];
-        load_row32_f16(p.resid, p.ld_resid, row, col, p.M, p.N, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = r[i] + h2f_round(v[i]);
+    for (int cp = 0; cp < 2; ++cp) {
+      const int c0 = half * 4 + cp * 2;  // first of two 32-column chunks
+      const int col0 = nb * BN + c0 * 32;
+      if (col0 >= p.N) break;
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tl + c0 * 32, r0);
+      tmem_ld32(tl + c0 * 32 + 32, r1);
+      uint4 q0[4], q1[4];
+      if (EPI == kF16 && p.resid) {
+        load_raw32(p.resid, p.ld_resid, row, col0, p.M, p.N, q0);
+        load_raw32(p.resid, p.ld_resid, row, col0 + 32, p.M, p.N, q1);
       }
-      store_row32_f16(p.C, p.ldc, row, col, p.M, p.N, v);
+      tmem_ld_wait();
+      float v0[32], v1[32];
+      to_f32(r0, v0);
+      to_f32(r1, v1);
+      if constexpr (EPI == kF16) {
+        if (p.resid) {
+          float a[32], b[32];
+          unpack32(q0, a);
+          unpack32(q1, b);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v0[i] = a[i] + h2f_round(v0[i]);
+            v1[i] = b[i] + h2f_round(v1[i]);
+          }
+        }
+        store_row32_f16(p.C, p.ldc, row, col0, p.M, p.N, v0);
+        store_row32_f16(p.C, p.ldc, row, col0 + 32, p.M, p.N, v1);
+      } else {
+        if (row >= p.M) continue;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const int col = col0 + part * 32;
+          const float* v = part ? v1 : v0;
+          if (p.splits > 1) {
+            float* dst = p.ws + ((int64_t)split * p.M + row) * p.N + col;
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              if (col + g * 4 + 4 <= p.N)
+                *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
+          } else {
+            float* dst = p.G + (int64_t)row * p.ldg + col;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              if (col + g * 4 + 4 <= p.N) {
+                float4 o = make_float4(h2f_round(v[g * 4]), h2f_round(v[g * 4 + 1]), h2f_round(v[g * 4 + 2]),
+                                       h2f_round(v[g * 4 + 3]));
+                if (p.accumulate) {
+                  const float4 old = *reinterpret_cast<const float4*>(dst + g * 4);
+                  o.x += old.x;
+                  o.y += old.y;
+                  o.z += old.z;
+                  o.w += old.w;
+                }
+                *reinterpret_cast<float4*>(dst + g * 4) = o;
+              }
+            }
+          }
+        }
+      }
     }
   } else if constexpr (EPI == kRope) {
     const int pos = p.rope_seq > 0 ? row % p.rope_seq : 0;
 #pragma unroll 1
-    for (int h = 0; h < BN / 64; ++h) {
+    for (int hh = 0; hh < 2; ++hh) {
+      const int h = half * 2 + hh;
       const int col = nb * BN + h * 64;
       if (col >= p.N) break;
+      uint32_t ra[32], rb[32];
+      tmem_ld32(tl + h * 64, ra);
+      tmem_ld32(tl + h * 64 + 32, rb);
+      tmem_ld_wait();
       float a[32], b[32];
-      tmem_load32f(tl + h * 64, a);
-      tmem_load32f(tl + h * 64 + 32, b);
+      to_f32(ra, a);
+      to_f32(rb, b);
       if (col < p.rope_cols && row < p.M) {
-        const float* cs = p.rope_cos + (int64_t)pos * 32;
-        const float* sn = p.rope_sin + (int64_t)pos * 32;
+        const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + (int64_t)pos * 32);
+        const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + (int64_t)pos * 32);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x0 = h2f_round(a[i]);
-          const float x1 = h2f_round(b[i]);
-          const float c_ = __ldg(cs + i), s_ = __ldg(sn + i);
-          a[i] = __fsub_rn(__fmul_rn(x0, c_), __fmul_rn(x1, s_));
-          b[i] = __fadd_rn(__fmul_rn(x0, s_), __fmul_rn(x1, c_));
+        for (int i4 = 0; i4 < 8; ++i4) {
+          const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+          const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int i = i4 * 4 + j;
+            const float x0 = h2f_round(a[i]);
+            const float x1 = h2f_round(b[i]);
+            a[i] = __fsub_rn(__fmul_rn(x0, cc[j]), __fmul_rn(x1, ss[j]));
+            b[i] = __fadd_rn(__fmul_rn(x0, ss[j]), __fmul_rn(x1, cc[j]));
+          }
         }
       }
       store_row32_f16(p.C, p.ldc, row, col, p.M, p.N, a);
@@ -194,16 +269,19 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, in
   } else if constexpr (EPI == kSwigluF) {
     const int F = p.swiglu_F;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int j = 0; j < 2; ++j) {
+      const int c = half * 2 + j;
       const int col = nb * 128 + c * 32;
       if (col >= F) break;
+      uint32_t rg[32], ru[32];
+      tmem_ld32(tl + c * 32, rg);
+      tmem_ld32(tl + 128 + c * 32, ru);
+      tmem_ld_wait();
       float g[32], u[32];
-      tmem_load32f(tl + c * 32, g);
-      tmem_load32f(tl + 128 + c * 32, u);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        g[i] = h2f_round(g[i]);
-        u[i] = h2f_round(u[i]);
+        g[i] = h2f_round(__uint_as_float(rg[i]));
+        u[i] = h2f_round(__uint_as_float(ru[i]));
       }
       store_row32_f16(p.C, p.ld_out, row, col, p.M, F, g);
       store_row32_f16(p.out1, p.ld_out, row, col, p.M, F, u);
@@ -214,57 +292,37 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, in
   } else if constexpr (EPI == kSwigluB) {
     const int F = p.swiglu_F;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int col = nb * BN + c * 32;
-      if (col >= F) break;
-      float d[32], g[32], u[32];
-      tmem_load32f(tl + c * 32, d);
-      load_row32_f16(p.aux0, p.ld_aux, row, col, p.M, F, g);
-      load_row32_f16(p.aux1, p.ld_aux, row, col, p.M, F, u);
-      float du[32];
+    for (int cp = 0; cp < 2; ++cp) {
+      const int c0 = half * 4 + cp * 2;
+      const int col0 = nb * BN + c0 * 32;
+      if (col0 >= F) break;
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tl + c0 * 32, r0);
+      tmem_ld32(tl + c0 * 32 + 32, r1);
+      uint4 g0[4], g1[4], u0[4], u1[4];
+      load_raw32(p.aux0, p.ld_aux, row, col0, p.M, F, g0);
+      load_raw32(p.aux0, p.ld_aux, row, col0 + 32, p.M, F, g1);
+      load_raw32(p.aux1, p.ld_aux, row, col0, p.M, F, u0);
+      load_raw32(p.aux1, p.ld_aux, row, col0 + 32, p.M, F, u1);
+      tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float d16 = h2f_round(d[i]);
-        const float s16 = h2f_round(silu_f(g[i]));
-        du[i] = __fmul_rn(d16, s16);
-        const float ds = h2f_round(__fmul_rn(d16, u[i]));
-        const float sig = __fdiv_rn(1.0f, 1.0f + expf(-g[i]));
-        d[i] = __fmul_rn(__fmul_rn(ds, sig), 1.0f + __fmul_rn(g[i], 1.0f - sig));
-      }
-      store_row32_f16(p.C, p.ldc, row, col, p.M, F, d);
-      store_row32_f16(p.C + F, p.ldc, row, col, p.M, F, du);
-    }
-  } else if constexpr (EPI == kWgrad) {
-#pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int col = nb * BN + c * 32;
-      if (col >= p.N) break;
-      float v[32];
-      tmem_load32f(tl + c * 32, v);
-      if (row >= p.M) continue;
-      if (p.splits > 1) {
-        float* dst = p.ws + ((int64_t)split * p.M + row) * p.N + col;
+      for (int part = 0; part < 2; ++part) {
+        float d[32], g[32], u[32], du[32];
+        to_f32(part ? r1 : r0, d);
+        unpack32(part ? g1 : g0, g);
+        unpack32(part ? u1 : u0, u);
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
-          if (col + g * 4 + 4 <= p.N)
-            *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
-      } else {
-        float* dst = p.G + (int64_t)row * p.ldg + col;
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          if (col + g * 4 + 4 <= p.N) {
-            float4 o = make_float4(h2f_round(v[g * 4]), h2f_round(v[g * 4 + 1]), h2f_round(v[g * 4 + 2]),
-                                   h2f_round(v[g * 4 + 3]));
-            if (p.accumulate) {
-              float4 old = *reinterpret_cast<float4*>(dst + g * 4);
-              o.x += old.x;
-              o.y += old.y;
-              o.z += old.z;
-              o.w += old.w;
-            }
-            *reinterpret_cast<float4*>(dst + g * 4) = o;
-          }
+        for (int i = 0; i < 32; ++i) {
+          const float d16 = h2f_round(d[i]);
+          const float sig = sigmoid_f(g[i]);
+          const float s16 = h2f_round(g[i] * sig);
+          du[i] = __fmul_rn(d16, s16);
+          const float ds = h2f_round(__fmul_rn(d16, u[i]));
+          d[i] = __fmul_rn(__fmul_rn(ds, sig), 1.0f + __fmul_rn(g[i], 1.0f - sig));
         }
+        const int col = col0 + part * 32;
+        store_row32_f16(p.C, p.ldc, row, col, p.M, F, d);
+        store_row32_f16(p.C + F, p.ldc, row, col, p.M, F, du);
       }
     }
   }
@@ -295,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -392,7 +450,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int quarter = warp & 3;        // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;    // which half of the tile's columns
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int mb, nb, s;
@@ -400,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int acc = local & 1;
       if (!wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
-      epilogue_tile<EPI>(p, tmem_base + acc * BN, quarter, lane, mb, nb, s);
+      epilogue_tile<EPI>(p, tmem_base + acc * BN, quarter, half, lane, mb, nb, s);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);

@@ -20,20 +20,24 @@ constexpr int kWarps = 8;
 constexpr int kMaxParts = 296;
 
 __device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
-  half8 h = *reinterpret_cast<const half8*>(p);
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    float2 f = __half22float2(h.h[j]);
+    float2 f = __half22float2(h[j]);
     v[2 * j] = f.x;
     v[2 * j + 1] = f.y;
   }
 }
 
 __device__ __forceinline__ void store8(__half* p, const float (&v)[8]) {
-  half8 h;
+  uint32_t w[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) h.h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-  *reinterpret_cast<half8*>(p) = h;
+  for (int j = 0; j < 4; ++j) {
+    __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    w[j] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 __device__ __forceinline__ float r16(float x) { return __half2float(__float2half_rn(x)); }
@@ -85,8 +89,13 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_kernel(const __half* 
   }
 }
 
+__device__ __forceinline__ float2 h2f2(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
 // dx = f16(dresid + f16(rstd * (gh - xhat * mean(gh * xhat)))), gh = f16(dy * gamma),
-// xhat = x * rstd; dgamma partial += dy * f16(xhat).
+// xhat = x * rstd; dgamma partial += dy * f16(xhat). Rows are held as packed
+// fp16 (4 registers per 8 values) to keep occupancy high.
 template <int NV>
 __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __half* __restrict__ dy,
                                                                   const __half* __restrict__ x,
@@ -107,24 +116,31 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __half* 
 
   for (int64_t row = blockIdx.x * (int64_t)kWarps + warp; row < rows; row += (int64_t)gridDim.x * kWarps) {
     const float rs = rstd[row];
-    float xv[NV][8], gv[NV][8];
+    uint4 xq[NV], dq[NV], rq[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < cols) {
+        dq[i] = *reinterpret_cast<const uint4*>(dy + row * cols + c);
+        xq[i] = *reinterpret_cast<const uint4*>(x + row * cols + c);
+        if (dresid) rq[i] = *reinterpret_cast<const uint4*>(dresid + row * cols + c);
+      }
+    }
     float dot = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = (i * 32 + lane) * 8;
       if (c < cols) {
-        float d[8];
-        load8(dy + row * cols + c, d);
-        load8(x + row * cols + c, xv[i]);
-        const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
-        const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
-        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const uint32_t* xw = &xq[i].x;
+        const uint32_t* dw = &dq[i].x;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float xh = xv[i][j] * rs;
-          dg[i][j] += d[j] * r16(xh);
-          gv[i][j] = r16(d[j] * g[j]);
-          dot += gv[i][j] * xh;
+        for (int j = 0; j < 4; ++j) {
+          const float2 xf = h2f2(xw[j]), df = h2f2(dw[j]);
+          const float2 g = *reinterpret_cast<const float2*>(gamma + c + 2 * j);
+          const float xh0 = xf.x * rs, xh1 = xf.y * rs;
+          dg[i][2 * j] += df.x * r16(xh0);
+          dg[i][2 * j + 1] += df.y * r16(xh1);
+          dot += r16(df.x * g.x) * xh0 + r16(df.y * g.y) * xh1;
         }
       }
     }
@@ -133,16 +149,25 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __half* 
     for (int i = 0; i < NV; ++i) {
       const int c = (i * 32 + lane) * 8;
       if (c < cols) {
-        float o[8];
-        float r[8];
-        if (dresid) load8(dresid + row * cols + c, r);
+        const uint32_t* xw = &xq[i].x;
+        const uint32_t* dw = &dq[i].x;
+        const uint32_t* rw = &rq[i].x;
+        uint32_t o[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float xh = xv[i][j] * rs;
-          o[j] = r16(rs * (gv[i][j] - xh * dot));
-          if (dresid) o[j] += r[j];
+        for (int j = 0; j < 4; ++j) {
+          const float2 xf = h2f2(xw[j]), df = h2f2(dw[j]);
+          const float2 g = *reinterpret_cast<const float2*>(gamma + c + 2 * j);
+          float o0 = r16(rs * (r16(df.x * g.x) - xf.x * rs * dot));
+          float o1 = r16(rs * (r16(df.y * g.y) - xf.y * rs * dot));
+          if (dresid) {
+            const float2 rf = h2f2(rw[j]);
+            o0 += rf.x;
+            o1 += rf.y;
+          }
+          __half2 h = __floats2half2_rn(o0, o1);
+          o[j] = *reinterpret_cast<uint32_t*>(&h);
         }
-        store8(dx + row * cols + c, o);
+        *reinterpret_cast<uint4*>(dx + row * cols + c) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
   }
@@ -163,13 +188,24 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __half* 
   }
 }
 
-__global__ void dgamma_reduce_kernel(const float* __restrict__ part, int nparts, int cols, float* __restrict__ dgamma,
-                                     int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+// dgamma[c] (+)= sum_p part[p][c]: 32 columns x 8 part-groups per block,
+// deterministic order (fixed partition, fixed tree).
+__global__ void __launch_bounds__(256) dgamma_reduce_kernel(const float* __restrict__ part, int nparts, int cols,
+                                                            float* __restrict__ dgamma, int accumulate) {
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
   float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[(int64_t)p * cols + c];
-  dgamma[c] = accumulate ? dgamma[c] + s : s;
+  if (c < cols)
+    for (int p = ty; p < nparts; p += 8) s += part[(int64_t)p * cols + c];
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][tx];
+    dgamma[c] = accumulate ? dgamma[c] + t : t;
+  }
 }
 
 template <template <int> class K>
@@ -261,7 +297,7 @@ extern "C" int jx_rmsnorm_bwd(const void* dy, const void* x, const float* rstd, 
 extern "C" int jx_rmsnorm_dgamma_reduce(const float* dgamma_part, int nparts, int cols, float* dgamma, int accumulate,
                                         jx_stream_t stream) {
   JX_CHECK_ARG(dgamma_part && dgamma && nparts > 0 && cols > 0, "jx_rmsnorm_dgamma_reduce: bad argument");
-  dgamma_reduce_kernel<<<(cols + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  dgamma_reduce_kernel<<<(cols + 31) / 32, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       dgamma_part, nparts, cols, dgamma, accumulate);
   JX_CHECK_LAUNCH("jx_rmsnorm_dgamma_reduce");
   return JX_OK;

@@ -77,8 +77,8 @@ class RuntimePlan:
 def build_runtime_plan(accelerators, launch: LaunchEnvironment | None = None) -> RuntimePlan:
     """cuda -> NCCL on cuda:LOCAL_RANK; cpu -> gloo. Mixed accelerators are rejected."""
     launch = launch or LaunchEnvironment()
-    requested = (accelerators,) if isinstance(accelerators, str) else tuple(accelerators)
-    requested = tuple(dict.fromkeys(a.strip().lower() for a in requested))
+    items = accelerators.split(",") if isinstance(accelerators, str) else list(accelerators)
+    requested = tuple(dict.fromkeys(a.strip().lower() for a in items if a.strip()))
     if requested == ("auto",):
         requested = ("cuda" if torch.cuda.is_available() else "cpu",)
     if len(requested) != 1:
