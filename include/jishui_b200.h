@@ -12,8 +12,9 @@
  *     the most recent failure on the calling thread is returned by
  *     jx_last_error().
  *   - The library allocates no device memory on any call. Scratch space (the
- *     split-K partials of the weight-gradient GEMM) is passed in by the
- *     caller; jx_gemm_wgrad_workspace_bytes() gives its size.
+ *     split-K partials of the weight-gradient GEMM, the attention backward's
+ *     dQ accumulator) is passed in by the caller; the *_workspace_bytes()
+ *     queries give its size.
  *
  * Reference interfaces replaced (paths are inside the Midstream-LLM project):
  *   src/jishui/model_torch.py:12-15   nn.RMSNorm            -> jx_rmsnorm_fwd / jx_rmsnorm_bwd
@@ -117,13 +118,17 @@ int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_t ldx, int 
 
 /* ---- Causal attention (model_torch.py:48, SDPA is_causal=True) ----
  * qkv: f16 [B*T, 3*H*D] rows (q | k | v, head h at column h*D of each part).
- * out: f16 [B*T, H*D]. lse: f32 [B, H, T] (natural-log logsumexp of the scaled scores). */
+ * out: f16 [B*T, H*D]. lse: f32 [B, H, T] (natural-log logsumexp of the scaled scores).
+ * D must be 64; T a multiple of 256 (forward) / 128 (backward). */
 int jx_attn_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int D, float scale,
                 jx_stream_t stream);
-/* Backward: writes dqkv f16 [B*T, 3*H*D]; delta is f32 [B, H, T] scratch.
+/* Backward: writes dqkv f16 [B*T, 3*H*D]. `workspace` is caller scratch of
+ * jx_attn_bwd_workspace_bytes(B, T, H, D) bytes (the row sums dO.O and an fp32
+ * dQ accumulator; the call clears what must start at zero).
  * If rope_cos/rope_sin are non-NULL the q/k gradients are rotated back
  * through RoPE (the inverse rotation) before they are stored. */
-int jx_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, float* delta, void* dqkv,
+int64_t jx_attn_bwd_workspace_bytes(int B, int T, int H, int D);
+int jx_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, void* workspace, void* dqkv,
                 int B, int T, int H, int D, float scale, const float* rope_cos, const float* rope_sin,
                 jx_stream_t stream);
 

@@ -1,0 +1,714 @@
+// Causal flash attention on the 5th-generation tensor cores (tcgen05),
+// head_dim 64: forward and backward.
+//
+// Reference: Midstream-LLM src/jishui/model_torch.py:48,
+// F.scaled_dot_product_attention(q, k, v, is_causal=True), scale 1/sqrt(64),
+// fp16 operands, fp32 softmax; the forward saves O and the natural-log LSE per
+// row, the backward recomputes the probabilities from them.
+//
+// Forward: one CTA per pair of 128-query tiles (A = 2p, B = 2p+1) of one
+// (head, batch), 320 threads:
+//   warp 0     TMA producer: Q_A, Q_B once, then K_j / V_j (128 keys) into a 3-stage ring,
+//   warp 1     TMEM allocator + MMA issuer, ping-ponging the two tiles:
+//                S_w = Q_w K_j^T (M 128, N 128, K 64) -> TMEM, O_w = P_w V_j (M 128, N 64, K 128),
+//   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B (one query row per
+//              thread): row max over the TMEM S row, fold the previous O_w into
+//              the fp32 output registers with the running rescale, P_w (fp16)
+//              into 128B-swizzled shared memory (the K-major A operand of P V).
+// While one warpgroup runs its softmax the tensor core works on the other's tile.
+// q/k/v are read in place from the fused projection output [B*T, 3*H*64] by
+// one TMA descriptor; O is written token-major [B*T, H*64].
+#include "jx_common.cuh"
+#include "jx_host.h"
+
+namespace jx {
+namespace fa {
+
+constexpr int D = 64;
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int KV_STAGES = 3;
+constexpr int kThreads = 320;
+constexpr uint32_t kTileBytes = BKV * D * 2;  // 16 KiB (one [128 x 64] fp16 tile)
+constexpr uint32_t kPBytes = BQ * BKV * 2;    // 32 KiB
+constexpr uint32_t kTmemCols = 512;
+// smem: Q_A, Q_B | K stages | V stages | P_A, P_B | barriers
+constexpr size_t kSmemBytes = 1024 + 2 * kTileBytes + 2 * KV_STAGES * kTileBytes + 2 * kPBytes + 512;
+
+enum Status : int { kFaProducer = 301, kFaMma = 302, kFaSoftmax = 303 };
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
+  uint64_t s_full[2], s_free[2], p_full[2], p_empty[2];  // per query tile (A, B)
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status, int code) {
+  const long long start = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      if (*abort_flag) return false;
+      if (clock64() - start > (1ll << 32)) {
+        *abort_flag = 1;
+        if (status) atomicExch(status, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __half* __restrict__ out, float* __restrict__ lse,
+                       int T, int H, float scale_log2, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                         // [2] query tiles
+  uint8_t* sK = sQ + 2 * kTileBytes;
+  uint8_t* sV = sK + KV_STAGES * kTileBytes;
+  uint8_t* sP = sV + KV_STAGES * kTileBytes;  // [2] P tiles
+  Bars* bars = reinterpret_cast<Bars*>(sP + 2 * kPBytes);
+  volatile int* abort_flag = &bars->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npairs = T / (2 * BQ);
+  const int pr = npairs - 1 - blockIdx.x;  // heaviest pair first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int d = H * D;
+  const int row_base = b * T;
+  const int nkv[2] = {2 * pr + 1, 2 * pr + 2};  // key tiles of query tiles A = 2pr and B = 2pr+1
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&bars->kv_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&bars->s_full[w], 1);
+      mbar_init(&bars->s_free[w], 4);
+      mbar_init(&bars->p_full[w], 4);
+      mbar_init(&bars->p_empty[w], 1);
+    }
+    bars->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  // TMEM columns of tile w: S at w*256 + [0,128), O at w*256 + [128,192).
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      mbar_expect_tx(&bars->q_full, 2 * kTileBytes);
+      tma_load_2d(sQ, &tm_qkv, &bars->q_full, h * D, row_base + (2 * pr) * BQ);
+      tma_load_2d(sQ + kTileBytes, &tm_qkv, &bars->q_full, h * D, row_base + (2 * pr + 1) * BQ);
+      for (int j = 0; j < nkv[1]; ++j) {
+        const int s = j % KV_STAGES;
+        if (!wait(&bars->kv_empty[s], ((j / KV_STAGES) & 1) ^ 1, abort_flag, status, kFaProducer)) break;
+        mbar_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
+        tma_load_2d(sK + s * kTileBytes, &tm_qkv, &bars->kv_full[s], d + h * D, row_base + j * BKV);
+        tma_load_2d(sV + s * kTileBytes, &tm_qkv, &bars->kv_full[s], 2 * d + h * D, row_base + j * BKV);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV, false, false);
+      constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
+      bool ok = wait(&bars->q_full, 0, abort_flag, status, kFaMma);
+      auto issue_s = [&](int w, int j) -> bool {
+        const int s = j % KV_STAGES;
+        if (!wait(&bars->kv_full[s], (j / KV_STAGES) & 1, abort_flag, status, kFaMma)) return false;
+        if (!wait(&bars->s_free[w], (j & 1) ^ 1, abort_flag, status, kFaMma)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + w * kTileBytes);
+        const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16(tmem + w * 256, smem_desc_sw128(q_addr + kk * 32, 16, 1024),
+                   smem_desc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(&bars->s_full[w]);
+        return true;
+      };
+      auto issue_pv = [&](int w, int j) -> bool {
+        const int s = j % KV_STAGES;
+        if (!wait(&bars->p_full[w], j & 1, abort_flag, status, kFaMma)) return false;
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sP + w * kPBytes);
+        const uint32_t v_addr = smem_u32(sV + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          // P: K-major [128 q x 128 keys] as two 64-key halves of 16 KiB each.
+          const uint64_t a = smem_desc_sw128(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          // V: [128 keys x 64 hd] read MN-major (hd contiguous), 16 keys = two 8-row groups.
+          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
+          umma_f16(tmem + w * 256 + 128, a, bdesc, idesc_o, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars->p_empty[w]);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
+      for (int j = 0; j < nkv[1] && ok; ++j) {
+        if (j < nkv[0]) {
+          if (!issue_pv(0, j)) break;
+          if (j + 1 < nkv[0] && !issue_s(0, j + 1)) break;
+        }
+        if (!issue_pv(1, j)) break;
+        umma_commit(&bars->kv_empty[j % KV_STAGES]);
+        if (j + 1 < nkv[1] && !issue_s(1, j + 1)) break;
+      }
+    }
+  } else {
+    // Softmax: warpgroup w (0: warps 2-5, 1: warps 6-9); thread owns query row r of its tile.
+    const int w = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qt = 2 * pr + w;  // query tile index
+    const int q = qt * BQ + r;  // position in the sequence
+    const int n = nkv[w];
+    const uint32_t lane_base = tmem + w * 256 + (static_cast<uint32_t>(quarter * 32) << 16);
+    float m = -INFINITY, l = 0.f;
+    float o[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n && ok; ++j) {
+      if (!wait(&bars->s_full[w], j & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = (j == n - 1);
+      // pass 1: row max over the 128 raw scores (only the diagonal tile is masked)
+      float mx = -INFINITY;
+      if (!diag) {
+#pragma unroll
+        for (int c = 0; c < BKV / 32; ++c) {
+          uint32_t sr[32];
+          tmem_ld32(lane_base + c * 32, sr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(sr[i]), __uint_as_float(sr[i + 1])));
+        }
+      } else {
+        const int lim = q - j * BKV;  // keys of this tile at column index <= lim are visible
+#pragma unroll
+        for (int c = 0; c < BKV / 32; ++c) {
+          uint32_t sr[32];
+          tmem_ld32(lane_base + c * 32, sr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, (c * 32 + i <= lim) ? __uint_as_float(sr[i]) : -INFINITY);
+        }
+      }
+      const float m_new = fmaxf(m, mx * scale_log2);
+      const float alpha = ex2(m - m_new);
+      m = m_new;
+      // fold O_{j-1} (scale m_{j-1}) and move to scale m_j; P buffer is then free
+      if (j > 0) {
+        if (!wait(&bars->p_empty[w], (j - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t orr[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld32(lane_base + 128 + half * 32, orr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[half * 32 + i] = (o[half * 32 + i] + __uint_as_float(orr[i])) * alpha;
+        }
+      }
+      // pass 2: P = exp2(s*scale - m) into the swizzled K-major layout (row r, 16 chunks of 8 keys)
+      float sum = 0.f;
+      const float neg_m = -m_new;
+      const int lim = diag ? q - j * BKV : BKV;
+      uint8_t* prow = sP + w * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int c4 = 0; c4 < BKV / 32; ++c4) {
+        uint32_t sr[32];
+        tmem_ld32(lane_base + c4 * 32, sr);
+        tmem_ld_wait();
+        float pv[32];
+        if (!diag) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pv[i] = ex2(fmaf(__uint_as_float(sr[i]), scale_log2, neg_m));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            pv[i] = (c4 * 32 + i <= lim) ? ex2(fmaf(__uint_as_float(sr[i]), scale_log2, neg_m)) : 0.f;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = pv[cc * 8 + 2 * e], p1 = pv[cc * 8 + 2 * e + 1];
+            sum += p0 + p1;
+            __half2 hp = __floats2half2_rn(p0, p1);
+            wv[e] = *reinterpret_cast<uint32_t*>(&hp);
+          }
+          const int c = c4 * 4 + cc;  // 16-byte chunk index, 0..15
+          const int half = c >> 3, ch = c & 7;
+          *reinterpret_cast<uint4*>(prow + half * 16384 + ((ch ^ (r & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+      }
+      l = l * alpha + sum;
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars->s_free[w]);
+        mbar_arrive(&bars->p_full[w]);
+      }
+    }
+    if (ok) {
+      // last P V
+      if (!wait(&bars->p_empty[w], (n - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
+    }
+    if (ok) {
+      tc_fence_after();
+      uint32_t orr[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld32(lane_base + 128 + half * 32, orr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[half * 32 + i] += __uint_as_float(orr[i]);
+      }
+      const float inv = 1.f / l;
+      __half* dst = out + (int64_t)(row_base + q) * d + h * D;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        uint32_t wv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __half2 hv = __floats2half2_rn(o[c * 8 + 2 * e] * inv, o[c * 8 + 2 * e + 1] * inv);
+          wv[e] = *reinterpret_cast<uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      }
+      lse[((int64_t)b * H + h) * T + q] = (m + __log2f(l)) * 0.69314718055994530942f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward on tcgen05. One CTA per (128-key block, head, batch); the key
+// block's K and V stay in shared memory, dK and dV accumulate in TMEM across
+// the query tiles i = kb .. T/128-1. Per query tile (Q_i, dO_i, LSE_i, Delta_i
+// double-buffered by TMA):
+//   S^T  = K Q_i^T     (M 128 keys, N 128 queries, K 64)   TMEM [0,128)
+//   dP^T = V dO_i^T    (M 128, N 128, K 64)                TMEM [128,256)
+//   softmax warps: P^T = exp(S^T*scale - LSE), dS^T = P^T (dP^T - Delta),
+//                  both fp16 into 128B-swizzled shared memory
+//   dV += P^T dO_i     (M 128, N 64, K 128; dO read MN-major)  TMEM [256,320)
+//   dK += dS^T Q_i     (M 128, N 64, K 128; Q read MN-major)   TMEM [320,384)
+//   dQ_i = dS K        (M 128 queries, N 64, K 128 keys; dS^T read MN-major
+//                       as the A operand, K read MN-major)     TMEM [384,512), two buffers
+//   dQ_i is added to an fp32 accumulator in global memory (vector reductions)
+//   while the MMAs of tile i+1 run.
+// Warps: 0 TMA producer, 1 MMA issuer, 2..9 softmax / epilogue (two warps per
+// TMEM lane quarter, each on half of the columns).
+// ---------------------------------------------------------------------------
+constexpr int kBwdThreads = 320;
+constexpr size_t kBwdSmem = 1024 + 2 * kTileBytes /*K,V*/ + 4 * kTileBytes /*Q,dO x2*/ + 2 * kPBytes /*P^T, dS^T*/ +
+                            2 * 2 * BQ * sizeof(float) /*LSE, Delta x2*/ + 512;
+
+struct BwdBars {
+  uint64_t kv_full;
+  uint64_t q_full[2], q_empty[2];
+  uint64_t sdp_full, sdp_free;
+  uint64_t p_full, grads_done, dq_free[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ float h16(float x) { return __half2float(__float2half_rn(x)); }
+
+// Inverse RoPE of one gradient pair (first-half column c, second-half column c+32) at position pos.
+__device__ __forceinline__ void rope_back(float& g1, float& g2, const float* cs, const float* sn, int pos, int c) {
+  const float co = __ldg(cs + (int64_t)pos * 32 + c), si = __ldg(sn + (int64_t)pos * 32 + c);
+  const float a = __fadd_rn(__fmul_rn(g1, co), __fmul_rn(g2, si));
+  const float b = __fsub_rn(__fmul_rn(g2, co), __fmul_rn(g1, si));
+  g1 = a;
+  g2 = b;
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                       const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq_acc,
+                       __half* __restrict__ dqkv, int T, int H, float scale, float scale_log2,
+                       const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kTileBytes;
+  uint8_t* sQ = sV + kTileBytes;             // 2 stages
+  uint8_t* sO = sQ + 2 * kTileBytes;         // dO, 2 stages
+  uint8_t* sPt = sO + 2 * kTileBytes;        // P^T  [128 keys x 128 queries]
+  uint8_t* sSt = sPt + kPBytes;              // dS^T [128 keys x 128 queries]
+  float* sL = reinterpret_cast<float*>(sSt + kPBytes);  // [2][128]
+  float* sD = sL + 2 * BQ;                               // [2][128]
+  BwdBars* bars = reinterpret_cast<BwdBars*>(sD + 2 * BQ);
+  volatile int* abort_flag = &bars->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = T / BQ;
+  const int kb = blockIdx.x;  // key block; kb = 0 has the most query tiles and starts first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int d = H * D;
+  const int row_base = b * T;
+  const int ntiles = nqb - kb;  // query tiles kb .. nqb-1
+  const float log2e = 1.4426950408889634f;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->q_full[s], 1);
+      mbar_init(&bars->q_empty[s], 1);
+    }
+    mbar_init(&bars->sdp_full, 1);
+    mbar_init(&bars->sdp_free, 8);
+    mbar_init(&bars->p_full, 8);
+    mbar_init(&bars->grads_done, 1);
+    mbar_init(&bars->dq_free[0], 8);
+    mbar_init(&bars->dq_free[1], 8);
+    bars->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  const float* lse_bh = lse + ((int64_t)b * H + h) * T;
+  const float* delta_bh = delta + ((int64_t)b * H + h) * T;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tm_do);
+      mbar_expect_tx(&bars->kv_full, 2 * kTileBytes);
+      tma_load_2d(sK, &tm_qkv, &bars->kv_full, d + h * D, row_base + kb * BKV);
+      tma_load_2d(sV, &tm_qkv, &bars->kv_full, 2 * d + h * D, row_base + kb * BKV);
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t & 1, qi = kb + t;
+        if (!wait(&bars->q_empty[s], ((t >> 1) & 1) ^ 1, abort_flag, status, kFaProducer)) break;
+        mbar_expect_tx(&bars->q_full[s], 2 * kTileBytes + 2 * BQ * sizeof(float));
+        tma_load_2d(sQ + s * kTileBytes, &tm_qkv, &bars->q_full[s], h * D, row_base + qi * BQ);
+        tma_load_2d(sO + s * kTileBytes, &tm_do, &bars->q_full[s], h * D, row_base + qi * BQ);
+        bulk_load(sL + s * BQ, lse_bh + qi * BQ, BQ * sizeof(float), &bars->q_full[s]);
+        bulk_load(sD + s * BQ, delta_bh + qi * BQ, BQ * sizeof(float), &bars->q_full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_sq = idesc_f16_f32(BKV, BQ, false, false);
+      constexpr uint32_t id_kn = idesc_f16_f32(BKV, D, false, true);
+      constexpr uint32_t id_q = idesc_f16_f32(BQ, D, true, true);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      const uint32_t pt_addr = smem_u32(sPt), st_addr = smem_u32(sSt);
+      bool ok = wait(&bars->kv_full, 0, abort_flag, status, kFaMma);
+      for (int t = 0; t < ntiles && ok; ++t) {
+        const int s = t & 1;
+        if (!wait(&bars->q_full[s], (t >> 1) & 1, abort_flag, status, kFaMma)) break;
+        if (!wait(&bars->sdp_free, (t & 1) ^ 1, abort_flag, status, kFaMma)) break;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), o_addr = smem_u32(sO + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16(tmem, smem_desc_sw128(k_addr + kk * 32, 16, 1024), smem_desc_sw128(q_addr + kk * 32, 16, 1024),
+                   id_sq, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 128, smem_desc_sw128(v_addr + kk * 32, 16, 1024),
+                   smem_desc_sw128(o_addr + kk * 32, 16, 1024), id_sq, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars->sdp_full);
+        if (!wait(&bars->p_full, t & 1, abort_flag, status, kFaMma)) break;
+        if (!wait(&bars->dq_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, status, kFaMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;  // K-major step over queries
+          umma_f16(tmem + 256, smem_desc_sw128(pt_addr + koff, 16, 1024), smem_desc_sw128(o_addr + kk * 2048, 8192, 1024),
+                   id_kn, (t > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tmem + 320, smem_desc_sw128(st_addr + koff, 16, 1024), smem_desc_sw128(q_addr + kk * 2048, 8192, 1024),
+                   id_kn, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          // dS^T read MN-major: queries contiguous (two 64-query halves 16 KiB apart), 16 keys per step.
+          umma_f16(tmem + 384 + (t & 1) * D, smem_desc_sw128(st_addr + kk * 2048, 16384, 1024),
+                   smem_desc_sw128(k_addr + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars->grads_done);
+        umma_commit(&bars->q_empty[s]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;         // TMEM lane quarter
+    const int colh = (warp - 2) >> 2;     // which half of the columns
+    const int r = quarter * 32 + lane;    // key row (S^T / dP^T / dK / dV) or query row (dQ)
+    const int key = kb * BKV + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    // dQ of query tile tp: TMEM lanes are query rows; this warp adds 32 of the 64 columns.
+    auto drain_dq = [&](int tp) {
+      const int buf = tp & 1;
+      tc_fence_after();
+      uint32_t qr[32];
+      tmem_ld32(lane_base + 384 + buf * D + colh * 32, qr);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->dq_free[buf]);
+      float* dst = dq_acc + (int64_t)(row_base + (kb + tp) * BQ + r) * d + h * D + colh * 32;
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        atomicAdd(reinterpret_cast<float4*>(dst + g * 4),
+                  make_float4(__uint_as_float(qr[g * 4]), __uint_as_float(qr[g * 4 + 1]),
+                              __uint_as_float(qr[g * 4 + 2]), __uint_as_float(qr[g * 4 + 3])));
+    };
+    bool ok = true;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const int s = t & 1, qi = kb + t;
+      const bool diag = (t == 0);
+      if (!wait(&bars->q_full[s], (t >> 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      if (!wait(&bars->sdp_full, t & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      const float* Ls = sL + s * BQ;
+      const float* Ds = sD + s * BQ;
+      // P^T and dS^T for this warp's 64 query columns, packed as fp16 pairs.
+      uint32_t pw[32], sw[32];
+      const int lim = diag ? key - qi * BQ : -1;  // on the diagonal tile, queries at index < lim... are masked
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(lane_base + colh * 64 + ch * 32, sr);
+        tmem_ld32(lane_base + 128 + colh * 64 + ch * 32, dr);
+        tmem_ld_wait();
+        const int q0 = colh * 64 + ch * 32;  // first query index of this chunk within the tile
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {  // 4 queries per group: LSE / Delta as float4 (broadcast reads)
+          const float4 L4 = *reinterpret_cast<const float4*>(Ls + q0 + g * 4);
+          const float4 D4 = *reinterpret_cast<const float4*>(Ds + q0 + g * 4);
+          const float nl[4] = {-L4.x * log2e, -L4.y * log2e, -L4.z * log2e, -L4.w * log2e};
+          const float dl[4] = {D4.x, D4.y, D4.z, D4.w};
+          float pv[4], dv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int qc = g * 4 + u;
+            float p = ex2(fmaf(__uint_as_float(sr[qc]), scale_log2, nl[u]));
+            if (diag && q0 + qc < lim) p = 0.f;
+            pv[u] = p;
+            dv[u] = p * (__uint_as_float(dr[qc]) - dl[u]);
+          }
+          __half2 hp0 = __floats2half2_rn(pv[0], pv[1]), hp1 = __floats2half2_rn(pv[2], pv[3]);
+          __half2 hs0 = __floats2half2_rn(dv[0], dv[1]), hs1 = __floats2half2_rn(dv[2], dv[3]);
+          pw[ch * 16 + g * 2] = *reinterpret_cast<uint32_t*>(&hp0);
+          pw[ch * 16 + g * 2 + 1] = *reinterpret_cast<uint32_t*>(&hp1);
+          sw[ch * 16 + g * 2] = *reinterpret_cast<uint32_t*>(&hs0);
+          sw[ch * 16 + g * 2 + 1] = *reinterpret_cast<uint32_t*>(&hs1);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->sdp_free);
+      // The previous tile's MMAs must be done reading P^T / dS^T before they are overwritten.
+      if (t > 0 && !wait(&bars->grads_done, (t - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      uint8_t* prow = sPt + colh * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
+      uint8_t* srow = sSt + colh * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 queries
+        const int off = (c ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[c * 4], pw[c * 4 + 1], pw[c * 4 + 2], pw[c * 4 + 3]);
+        *reinterpret_cast<uint4*>(srow + off) = make_uint4(sw[c * 4], sw[c * 4 + 1], sw[c * 4 + 2], sw[c * 4 + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full);
+      // The previous tile's dQ is complete (grads_done(t-1)); reduce it while this tile's MMAs run.
+      if (t > 0) drain_dq(t - 1);
+    }
+    if (ok && !wait(&bars->grads_done, (ntiles - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
+    if (ok) drain_dq(ntiles - 1);
+    if (ok) {
+      // dK (warps with colh 0, scaled, rotated back through RoPE) and dV (colh 1).
+      tc_fence_after();
+      uint32_t ar[64];
+      const uint32_t col = colh == 0 ? 320u : 256u;
+      tmem_ld32(lane_base + col, *reinterpret_cast<uint32_t(*)[32]>(&ar[0]));
+      tmem_ld32(lane_base + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&ar[32]));
+      tmem_ld_wait();
+      float v[64];
+      const float sc = colh == 0 ? scale : 1.0f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) v[i] = h16(__uint_as_float(ar[i]) * sc);
+      if (colh == 0 && rope_cos) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) rope_back(v[c], v[c + 32], rope_cos, rope_sin, key, c);
+      }
+      __half* dst = dqkv + (int64_t)(row_base + key) * (3 * d) + (colh == 0 ? d : 2 * d) + h * D;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __half2 hv = __floats2half2_rn(v[c * 8 + 2 * e], v[c * 8 + 2 * e + 1]);
+          w[e] = *reinterpret_cast<uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// dqkv[:, h*64 + c] = f16(RoPE^-1(f16(dq_acc * scale))) for the query part; one
+// thread per (row, head, group of 8 rotation pairs), 16-byte accesses.
+__global__ void attn_dq_finish_kernel(const float* __restrict__ dq_acc, __half* __restrict__ dqkv, int64_t rows, int H,
+                                      int T, float scale, const float* __restrict__ rope_cos,
+                                      const float* __restrict__ rope_sin) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t total = rows * H * 4;
+  if (i >= total) return;
+  const int grp = (int)(i & 3);
+  const int64_t rh = i >> 2;
+  const int h = (int)(rh % H);
+  const int64_t row = rh / H;
+  const int d = H * D;
+  const float* src = dq_acc + row * d + h * D + grp * 8;
+  float g1[8], g2[8];
+  const float4 a0 = *reinterpret_cast<const float4*>(src), a1 = *reinterpret_cast<const float4*>(src + 4);
+  const float4 b0 = *reinterpret_cast<const float4*>(src + 32), b1 = *reinterpret_cast<const float4*>(src + 36);
+  const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  const int pos = (int)(row % T);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    g1[j] = h16(av[j] * scale);
+    g2[j] = h16(bv[j] * scale);
+    if (rope_cos) rope_back(g1[j], g2[j], rope_cos, rope_sin, pos, grp * 8 + j);
+  }
+  uint32_t w1[4], w2[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __half2 x = __floats2half2_rn(g1[2 * e], g1[2 * e + 1]);
+    __half2 y = __floats2half2_rn(g2[2 * e], g2[2 * e + 1]);
+    w1[e] = *reinterpret_cast<uint32_t*>(&x);
+    w2[e] = *reinterpret_cast<uint32_t*>(&y);
+  }
+  __half* dst = dqkv + row * (3 * d) + h * D + grp * 8;
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+  *reinterpret_cast<uint4*>(dst + 32) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+}
+
+}  // namespace fa
+}  // namespace jx
+
+using namespace jx;
+using namespace jx::fa;
+
+extern "C" int jx_attn_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int Dh, float scale,
+                           jx_stream_t stream) {
+  JX_CHECK_ARG(qkv && out && lse, "jx_attn_fwd: NULL argument");
+  JX_CHECK_ARG(Dh == 64, "jx_attn_fwd: head_dim must be 64 (got %d)", Dh);
+  JX_CHECK_ARG(B > 0 && H > 0 && T > 0 && T % 256 == 0, "jx_attn_fwd: T must be a positive multiple of 256 (got %d)", T);
+  JX_CHECK_ARG(aligned16(qkv) && aligned16(out), "jx_attn_fwd: buffers must be 16-byte aligned");
+  const int64_t rows = (int64_t)B * T;
+  const int64_t cols = 3LL * H * D;
+  CUtensorMap tm;
+  JX_CHECK_ARG(make_tmap_f16(&tm, qkv, cols, rows, cols, D, BKV), "jx_attn_fwd: cannot encode TMA descriptor");
+  static bool attr_set = false;
+  if (!attr_set) {
+    JX_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes),
+                "jx_attn_fwd: smem attribute");
+    attr_set = true;
+  }
+  const float scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid(T / (2 * BQ), H, B);
+  attn_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
+      tm, static_cast<__half*>(out), lse, T, H, scale_log2, status_ptr());
+  JX_CHECK_LAUNCH("jx_attn_fwd");
+  return JX_OK;
+}
+
+extern "C" int64_t jx_attn_bwd_workspace_bytes(int B, int T, int H, int Dh) {
+  return (int64_t)B * H * T * 4 + (int64_t)B * T * H * Dh * 4;
+}
+
+// Delta = rowsum(dO * O), computed by attn_delta_kernel in attention.cu.
+namespace jx {
+namespace attn {
+void launch_delta(const __half* out, const __half* dout, float* delta, int B, int T, int H, cudaStream_t s);
+}
+}  // namespace jx
+
+extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, void* workspace,
+                           void* dqkv, int B, int T, int H, int Dh, float scale, const float* rope_cos,
+                           const float* rope_sin, jx_stream_t stream) {
+  JX_CHECK_ARG(qkv && out && dout && lse && workspace && dqkv, "jx_attn_bwd: NULL argument");
+  JX_CHECK_ARG(Dh == 64, "jx_attn_bwd: head_dim must be 64 (got %d)", Dh);
+  JX_CHECK_ARG(B > 0 && H > 0 && T > 0 && T % 128 == 0, "jx_attn_bwd: T must be a positive multiple of 128");
+  JX_CHECK_ARG(aligned16(qkv) && aligned16(out) && aligned16(dout) && aligned16(dqkv) && aligned16(lse) &&
+                   aligned16(workspace),
+               "jx_attn_bwd: buffers must be 16-byte aligned");
+  JX_CHECK_ARG((rope_cos == nullptr) == (rope_sin == nullptr), "jx_attn_bwd: pass both RoPE tables or neither");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float* delta = static_cast<float*>(workspace);
+  float* dq_acc = delta + (int64_t)B * H * T;
+  const int64_t rows = (int64_t)B * T;
+  const int d = H * D;
+  CUtensorMap tq, tdo;
+  JX_CHECK_ARG(make_tmap_f16(&tq, qkv, 3LL * d, rows, 3LL * d, D, BKV), "jx_attn_bwd: cannot encode TMA descriptor");
+  JX_CHECK_ARG(make_tmap_f16(&tdo, dout, d, rows, d, D, BQ), "jx_attn_bwd: cannot encode TMA descriptor");
+  JX_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)rows * d * sizeof(float), s), "jx_attn_bwd: clear dq accumulator");
+  jx::attn::launch_delta(static_cast<const __half*>(out), static_cast<const __half*>(dout), delta, B, T, H, s);
+  JX_CHECK_LAUNCH("jx_attn_bwd: delta");
+  static bool attr_set = false;
+  if (!attr_set) {
+    JX_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem),
+                "jx_attn_bwd: smem attribute");
+    attr_set = true;
+  }
+  dim3 grid(T / BKV, H, B);
+  attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, lse, delta, dq_acc, static_cast<__half*>(dqkv), T, H,
+                                                        scale, scale * 1.4426950408889634f, rope_cos, rope_sin,
+                                                        status_ptr());
+  JX_CHECK_LAUNCH("jx_attn_bwd");
+  const int64_t groups = rows * H * 4;
+  attn_dq_finish_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, s>>>(dq_acc, static_cast<__half*>(dqkv), rows, H, T,
+                                                                        scale, rope_cos, rope_sin);
+  JX_CHECK_LAUNCH("jx_attn_bwd: dq finish");
+  return JX_OK;
+}

@@ -42,7 +42,8 @@ constexpr uint32_t kABytes = BM * BK * 2;  // 16 KiB
 constexpr uint32_t kBBytes = BN * BK * 2;  // 32 KiB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemCols = 512;
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + STAGES * kStageBytes + 256 /*barriers*/;
+constexpr uint32_t kStageOutBytes = 32 * 128;  // one 32-row x 64-col fp16 output sub-tile per epilogue warp
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiWarps * kStageOutBytes + 256 /*barriers*/;
 
 enum Epi : int { kF16 = 0, kRope = 1, kSwigluF = 2, kSwigluB = 3, kWgrad = 4 };
 
@@ -159,14 +160,68 @@ __device__ __forceinline__ void to_f32(const uint32_t (&r)[32], float (&v)[32]) 
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
+// TMA store of one staged [32 rows x 64 cols] fp16 sub-tile (128B-swizzled).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Per-warp staging of output sub-tiles: thread `lane` owns staging row `lane`
+// (tile row 32q + lane); 64 fp16 columns = 8 16-byte chunks, XOR-swizzled by
+// row as the 128B-swizzled TMA box expects. One lane issues the TMA store.
+struct Stager {
+  uint8_t* buf;
+  int lane;
+  __device__ __forceinline__ void begin() {  // the previous store has finished reading the buffer
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+  }
+  __device__ __forceinline__ void put32(int part, const float (&v)[32]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        __half2 h = __floats2half2_rn(v[j * 8 + 2 * e], v[j * 8 + 2 * e + 1]);
+        w[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      const int c = part * 4 + j;
+      *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  __device__ __forceinline__ void flush(const CUtensorMap* map, int x, int y) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, buf, x, y);
+      bulk_commit();
+    }
+  }
+};
+
+struct OutMaps {
+  const CUtensorMap* c0;
+  const CUtensorMap* c1;
+  const CUtensorMap* c2;
+};
+
 // Epilogue of one 128 x 256 accumulator tile. Eight warps drain it: warp
 // quarter q (= warp % 4) owns TMEM lanes / tile rows [32q, 32q+32), and half
 // h owns half of the columns (for kSwigluF: half of the gate and of the up
-// columns; for kRope: two of the four heads). Each thread owns one row.
+// columns; for kRope: two of the four heads). Each thread owns one row; fp16
+// outputs go out through per-warp shared-memory staging and TMA stores
+// (out-of-range rows/columns are clipped by the tensor map), the fp32
+// weight-gradient output with direct 16-byte accesses.
 template <int EPI>
-__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, int quarter, int half, int lane, int mb,
-                                              int nb, int split) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om, Stager& st, uint32_t tacc,
+                                              int quarter, int half, int lane, int mb, int nb, int split) {
   const int row = mb * BM + quarter * 32 + lane;
+  const int yrow = mb * BM + quarter * 32;  // first row of this warp's TMA boxes
   const uint32_t tl = tacc + (static_cast<uint32_t>(quarter * 32) << 16);
   if constexpr (EPI == kF16 || EPI == kWgrad) {
 #pragma unroll 1
@@ -197,8 +252,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, in
             v1[i] = b[i] + h2f_round(v1[i]);
           }
         }
-        store_row32_f16(p.C, p.ldc, row, col0, p.M, p.N, v0);
-        store_row32_f16(p.C, p.ldc, row, col0 + 32, p.M, p.N, v1);
+        st.begin();
+        st.put32(0, v0);
+        st.put32(1, v1);
+        st.flush(om.c0, col0, yrow);
       } else {
         if (row >= p.M) continue;
 #pragma unroll
@@ -263,31 +320,46 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, in
           }
         }
       }
-      store_row32_f16(p.C, p.ldc, row, col, p.M, p.N, a);
-      store_row32_f16(p.C, p.ldc, row, col + 32, p.M, p.N, b);
+      st.begin();
+      st.put32(0, a);
+      st.put32(1, b);
+      st.flush(om.c0, col, yrow);
     }
   } else if constexpr (EPI == kSwigluF) {
     const int F = p.swiglu_F;
-#pragma unroll 1
-    for (int j = 0; j < 2; ++j) {
-      const int c = half * 2 + j;
-      const int col = nb * 128 + c * 32;
-      if (col >= F) break;
-      uint32_t rg[32], ru[32];
-      tmem_ld32(tl + c * 32, rg);
-      tmem_ld32(tl + 128 + c * 32, ru);
+    const int col = nb * 128 + half * 64;  // 64 gate columns (and the matching up columns)
+    if (col < F) {
+      uint32_t rg0[32], rg1[32], ru0[32], ru1[32];
+      tmem_ld32(tl + half * 64, rg0);
+      tmem_ld32(tl + half * 64 + 32, rg1);
+      tmem_ld32(tl + 128 + half * 64, ru0);
+      tmem_ld32(tl + 128 + half * 64 + 32, ru1);
       tmem_ld_wait();
-      float g[32], u[32];
+      float g0[32], g1[32], u0[32], u1[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        g[i] = h2f_round(__uint_as_float(rg[i]));
-        u[i] = h2f_round(__uint_as_float(ru[i]));
+        g0[i] = h2f_round(__uint_as_float(rg0[i]));
+        g1[i] = h2f_round(__uint_as_float(rg1[i]));
+        u0[i] = h2f_round(__uint_as_float(ru0[i]));
+        u1[i] = h2f_round(__uint_as_float(ru1[i]));
       }
-      store_row32_f16(p.C, p.ld_out, row, col, p.M, F, g);
-      store_row32_f16(p.out1, p.ld_out, row, col, p.M, F, u);
+      st.begin();
+      st.put32(0, g0);
+      st.put32(1, g1);
+      st.flush(om.c0, col, yrow);
+      st.begin();
+      st.put32(0, u0);
+      st.put32(1, u1);
+      st.flush(om.c1, col, yrow);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) g[i] = __fmul_rn(h2f_round(silu_f(g[i])), u[i]);
-      store_row32_f16(p.out2, p.ld_out, row, col, p.M, F, g);
+      for (int i = 0; i < 32; ++i) {
+        g0[i] = __fmul_rn(h2f_round(silu_f(g0[i])), u0[i]);
+        g1[i] = __fmul_rn(h2f_round(silu_f(g1[i])), u1[i]);
+      }
+      st.begin();
+      st.put32(0, g0);
+      st.put32(1, g1);
+      st.flush(om.c2, col, yrow);
     }
   } else if constexpr (EPI == kSwigluB) {
     const int F = p.swiglu_F;
@@ -305,9 +377,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, in
       load_raw32(p.aux1, p.ld_aux, row, col0, p.M, F, u0);
       load_raw32(p.aux1, p.ld_aux, row, col0 + 32, p.M, F, u1);
       tmem_ld_wait();
+      float dg[2][32], du[2][32];
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
-        float d[32], g[32], u[32], du[32];
+        float d[32], g[32], u[32];
         to_f32(part ? r1 : r0, d);
         unpack32(part ? g1 : g0, g);
         unpack32(part ? u1 : u0, u);
@@ -316,26 +389,34 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, in
           const float d16 = h2f_round(d[i]);
           const float sig = sigmoid_f(g[i]);
           const float s16 = h2f_round(g[i] * sig);
-          du[i] = __fmul_rn(d16, s16);
+          du[part][i] = __fmul_rn(d16, s16);
           const float ds = h2f_round(__fmul_rn(d16, u[i]));
-          d[i] = __fmul_rn(__fmul_rn(ds, sig), 1.0f + __fmul_rn(g[i], 1.0f - sig));
+          dg[part][i] = __fmul_rn(__fmul_rn(ds, sig), 1.0f + __fmul_rn(g[i], 1.0f - sig));
         }
-        const int col = col0 + part * 32;
-        store_row32_f16(p.C, p.ldc, row, col, p.M, F, d);
-        store_row32_f16(p.C + F, p.ldc, row, col, p.M, F, du);
       }
+      st.begin();
+      st.put32(0, dg[0]);
+      st.put32(1, dg[1]);
+      st.flush(om.c0, col0, yrow);
+      st.begin();
+      st.put32(0, du[0]);
+      st.put32(1, du[1]);
+      st.flush(om.c1, col0, yrow);
     }
   }
 }
 
 template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC0, const __grid_constant__ CUtensorMap tmC1,
+                const __grid_constant__ CUtensorMap tmC2, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint8_t* sOut = smem + STAGES * kStageBytes;  // kEpiWarps x 4 KiB output staging
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kEpiWarps * kStageOutBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;
@@ -452,6 +533,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int quarter = warp & 3;        // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;    // which half of the tile's columns
+    Stager st{sOut + (warp - 2) * kStageOutBytes, lane};
+    const OutMaps om{&tmC0, &tmC1, &tmC2};
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int mb, nb, s;
@@ -459,11 +542,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int acc = local & 1;
       if (!wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
-      epilogue_tile<EPI>(p, tmem_base + acc * BN, quarter, half, lane, mb, nb, s);
+      epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb, nb, s);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
+    if (lane == 0) bulk_wait_all();  // outstanding output stores complete before the CTA retires
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -563,6 +648,19 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
   else
     ok = make_tmap_f16(&tb, B, b_rows, p.K, ldb, 64, BK);
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for B", name);
+  // Output descriptors: [rows, cols] fp16 boxes of 32 rows x 64 columns (one epilogue warp's sub-tile).
+  CUtensorMap tc0 = ta, tc1 = ta, tc2 = ta;
+  if constexpr (EPI == kF16 || EPI == kRope) {
+    ok = make_tmap_f16(&tc0, p.C, p.N, p.M, p.ldc, 64, 32);
+  } else if constexpr (EPI == kSwigluF) {
+    ok = make_tmap_f16(&tc0, p.C, p.swiglu_F, p.M, p.ld_out, 64, 32) &&
+         make_tmap_f16(&tc1, p.out1, p.swiglu_F, p.M, p.ld_out, 64, 32) &&
+         make_tmap_f16(&tc2, p.out2, p.swiglu_F, p.M, p.ld_out, 64, 32);
+  } else if constexpr (EPI == kSwigluB) {
+    ok = make_tmap_f16(&tc0, p.C, p.swiglu_F, p.M, p.ldc, 64, 32) &&
+         make_tmap_f16(&tc1, p.C + p.swiglu_F, p.swiglu_F, p.M, p.ldc, 64, 32);
+  }
+  JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for the output", name);
 
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (EPI == kSwigluF) ? (p.swiglu_F + 127) / 128 : (p.N + BN - 1) / BN;
@@ -582,7 +680,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
   }
   const int tiles = p.tiles_m * p.tiles_n * p.splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_kernel<EPI, A_MN, B_MN><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  gemm_kernel<EPI, A_MN, B_MN><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tc0, tc1, tc2, p);
   JX_CHECK_LAUNCH(name);
   return JX_OK;
 }

@@ -242,7 +242,7 @@ class Workspace:
     do: torch.Tensor
     dqkv: torch.Tensor
     dgu: torch.Tensor
-    delta: torch.Tensor
+    attn_ws: torch.Tensor
     norm_part: torch.Tensor
     wgrad_ws: torch.Tensor
     cos: torch.Tensor
@@ -250,16 +250,21 @@ class Workspace:
     extra: dict = field(default_factory=dict)
 
 
-def _wgrad_splits(n: int, k: int, sms: int = 148) -> int:
-    """Split count for a weight-gradient GEMM with [n, k] output (128x256 tiles):
-    the smallest split that fills the SMs with the least wave tail."""
+def _wgrad_splits(n: int, k: int, tokens: int = 16384, sms: int = 148) -> int:
+    """Split count for a weight-gradient GEMM with [n, k] output (128x256 tiles)
+    reducing over `tokens`: minimises (waves x per-split main loop) + the split-K
+    partials' HBM round trip, with a per-SM rate of ~7.4 TFLOP/s and 6 TB/s."""
     tiles = -(-n // 128) * -(-k // 256)
-    best, best_eff = 1, 0.0
+    tile_us = 2.0 * 128 * 256 * tokens / 7.4e6  # one tile over all tokens, microseconds
+    best, best_t = 1, None
     for s in range(1, 9):
-        units = tiles * s
-        eff = (units / sms) / math.ceil(units / sms)
-        if eff > best_eff + 0.05:
-            best, best_eff = s, eff
+        if tokens // s < 1024:
+            break
+        t = math.ceil(tiles * s / sms) * tile_us / s
+        if s > 1:
+            t += (2.0 * s + 2.0) * n * k * 4 / 6e6
+        if best_t is None or t < best_t * 0.97:
+            best, best_t = s, t
     return best
 
 
@@ -314,7 +319,7 @@ class JishuiForCausalLM(nn.Module):
         wmax = 0
         if train:
             for n, k in ((3 * d, d), (d, d), (2 * F, d), (d, F), (c.vocab_size, d)):
-                s = _wgrad_splits(n, k)
+                s = _wgrad_splits(n, k, M)
                 wmax = max(wmax, ops.wgrad_workspace_bytes(n, k, s))
         xs_slots = L + 1 if train else 2
         ws = Workspace(
@@ -324,7 +329,7 @@ class JishuiForCausalLM(nn.Module):
             dx=torch.empty(M, d, **f16) if train else None, dxmid=torch.empty(M, d, **f16) if train else None,
             dh=torch.empty(M, d, **f16) if train else None, do=torch.empty(M, d, **f16) if train else None,
             dqkv=torch.empty(M, 3 * d, **f16) if train else None, dgu=torch.empty(M, 2 * F, **f16) if train else None,
-            delta=torch.empty(B, H, T, **f32) if train else None,
+            attn_ws=torch.empty(ops.attn_bwd_workspace_bytes(B, T, H, c.head_dim) // 4 + 4, **f32) if train else None,
             norm_part=torch.empty(nparts * d, **f32), wgrad_ws=torch.empty(max(wmax // 4, 4), **f32),
             cos=cos, sin=sin)
         self._ws[key] = ws
@@ -429,7 +434,7 @@ class JishuiForCausalLM(nn.Module):
         e16 = fl.p16_rows("embed_tokens.weight", V, d)
         ge = fl.g32_rows("embed_tokens.weight", V, d)
         ops.gemm_f16(ws.logits, e16, b_mn_major=True, out=ws.dh)
-        ops.gemm_wgrad(ws.logits, ws.hf, ge, accumulate, _wgrad_splits(V, d), ws.wgrad_ws)
+        ops.gemm_wgrad(ws.logits, ws.hf, ge, accumulate, _wgrad_splits(V, d, ws.B * ws.T), ws.wgrad_ws)
         x_last = ws.extra["x_last"]
         ops.rmsnorm_bwd(ws.dh, x_last, ws.rstdf, fl.p32_view("norm.weight", (d,)), out=ws.dx,
                         dgamma=fl.g32_view("norm.weight", (d,)), accumulate=accumulate, part=ws.norm_part)
@@ -454,18 +459,19 @@ class JishuiForCausalLM(nn.Module):
     def _layer_bwd(self, w, ws: Workspace, A: LayerActs, x_in: torch.Tensor, acc: bool) -> None:
         c = self.config
         B, T = ws.B, ws.T
+        M = B * T
         d, F, H, hd = c.hidden_size, c.intermediate_size, c.num_attention_heads, c.head_dim
         ops.gemm_swiglu_bwd(ws.dx, w["wd"], A.gate, A.up, out=ws.dgu)
-        ops.gemm_wgrad(ws.dx, A.act, w["gd"], acc, _wgrad_splits(d, F), ws.wgrad_ws)
+        ops.gemm_wgrad(ws.dx, A.act, w["gd"], acc, _wgrad_splits(d, F, M), ws.wgrad_ws)
         ops.gemm_f16(ws.dgu, w["wgu"], b_mn_major=True, out=ws.dh)
-        ops.gemm_wgrad(ws.dgu, A.h2, w["ggu"], acc, _wgrad_splits(2 * F, d), ws.wgrad_ws)
+        ops.gemm_wgrad(ws.dgu, A.h2, w["ggu"], acc, _wgrad_splits(2 * F, d, M), ws.wgrad_ws)
         ops.rmsnorm_bwd(ws.dh, A.xmid, A.rstd2, w["g2"], dresid=ws.dx, out=ws.dxmid, dgamma=w["gg2"], accumulate=acc,
                         part=ws.norm_part)
         ops.gemm_f16(ws.dxmid, w["wo"], b_mn_major=True, out=ws.do)
-        ops.gemm_wgrad(ws.dxmid, A.o, w["go"], acc, _wgrad_splits(d, d), ws.wgrad_ws)
-        ops.attn_bwd(A.qkv, A.o, ws.do, A.lse, B, T, H, hd, cos=ws.cos, sin=ws.sin, out=ws.dqkv, delta=ws.delta)
+        ops.gemm_wgrad(ws.dxmid, A.o, w["go"], acc, _wgrad_splits(d, d, M), ws.wgrad_ws)
+        ops.attn_bwd(A.qkv, A.o, ws.do, A.lse, B, T, H, hd, cos=ws.cos, sin=ws.sin, out=ws.dqkv, workspace=ws.attn_ws)
         ops.gemm_f16(ws.dqkv, w["wqkv"], b_mn_major=True, out=ws.dh)
-        ops.gemm_wgrad(ws.dqkv, A.h1, w["gqkv"], acc, _wgrad_splits(3 * d, d), ws.wgrad_ws)
+        ops.gemm_wgrad(ws.dqkv, A.h1, w["gqkv"], acc, _wgrad_splits(3 * d, d, M), ws.wgrad_ws)
         ops.rmsnorm_bwd(ws.dh, x_in, A.rstd1, w["g1"], dresid=ws.dxmid, out=ws.dx, dgamma=w["gg1"], accumulate=acc,
                         part=ws.norm_part)
 

@@ -227,11 +227,18 @@ def attn_fwd(qkv: torch.Tensor, B: int, T: int, H: int, D: int, out: torch.Tenso
     return o, lse
 
 
-def attn_bwd(qkv, o, do, lse, B, T, H, D, cos=None, sin=None, out=None, delta=None):
+def attn_bwd_workspace_bytes(B: int, T: int, H: int, D: int) -> int:
+    return _lib.query("jx_attn_bwd_workspace_bytes", B, T, H, D)
+
+
+def attn_bwd(qkv, o, do, lse, B, T, H, D, cos=None, sin=None, out=None, workspace=None):
+    """dqkv f16 [B*T, 3*H*D]; q/k gradients rotated back through RoPE when tables are given."""
     _check(do, F16, "do")
     dqkv = out if out is not None else torch.empty_like(qkv)
-    delta = delta if delta is not None else torch.empty(B, H, T, device=qkv.device, dtype=F32)
-    _lib.call("jx_attn_bwd", qkv.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
+    need = attn_bwd_workspace_bytes(B, T, H, D)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need // 4 + 4, device=qkv.device, dtype=F32)
+    _lib.call("jx_attn_bwd", qkv.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(), workspace.data_ptr(),
               dqkv.data_ptr(), B, T, H, D, 1.0 / math.sqrt(D), _ptr(cos), _ptr(sin), _stream())
     return dqkv
 
