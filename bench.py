@@ -295,8 +295,8 @@ def main() -> None:
             "config": {"workload": wl["name"], "model": cfg.name, "global_batch": B * accum * world, "micro_batch": B,
                        "grad_accum": accum, "seq_len": T, "parallelism": f"dp{world}",
                        "l2": "working set (activations, 953 MB fp32 grads) far exceeds the 126 MB L2"},
-            "mfu": value * f_model / (pk["bf16_tflops"] * 1e12),
-            "mfu_palm": value * f_palm / (pk["bf16_tflops"] * 1e12),
+            "mfu": value * f_model / (world * pk["bf16_tflops"] * 1e12),
+            "mfu_palm": value * f_palm / (world * pk["bf16_tflops"] * 1e12),
             "peak_kind": pk_kind,
             "roofline": {"kernel": "gemm_kernel (tcgen05, all GEMM launches of the timed updates)", "bound": "tensor",
                          "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",

@@ -1,0 +1,223 @@
+"""Operator microbenchmarks of the bandwidth-bound path and the dense kernels.
+
+    python -m midstream_llm_b200.microbench [--op all|rmsnorm|ce|adamw|gemm|attn] [--iters N]
+
+Shapes (the operator workload of the Jishui-200M step):
+  rmsnorm  fwd with residual add and bwd with residual gradient on fp16 [16384, 1024];
+           algorithmic bytes 4*M*d*2 = 134,217,728 each way (+ rstd / gamma)
+  ce       fused chunked cross-entropy: hidden [16384, 1024] x tied embedding
+           [32000, 1024], Zipf(1.1) labels: logits GEMM, CE fwd, CE bwd (in place),
+           dH and dE GEMMs = 3 x 2*M*V*d = 3.221 TFLOP; the softmax sub-steps are
+           also reported against the 2.097 GB an fp16 logits read + dlogits write costs
+  adamw    unscale + non-finite check + global norm + clip + AdamW over 200M fp32
+           parameters with fp16 gradients N(0, 1e-3): 28 B/param (5.6 GB); a flagged
+           step with 1 % +inf gradients runs the statistics pass only (2 B/param)
+  gemm     the decoder's GEMM shapes with their fused epilogues
+  attn     causal flash attention fwd / bwd at (B 16, T 1024) and (B 4, T 4096), 16 heads x 64
+Each line is JSON with the time per call (CUDA events, after warm-up, inputs
+larger than L2 unless noted) and the achieved rate against the measured peaks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+from . import ops
+from .data import ZipfBatches
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _peaks() -> dict:
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "fallback": True}
+
+
+def _time(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters / 1000.0  # seconds per call
+
+
+def _emit(name: str, seconds: float, work: float, unit: str, peak: float, **extra) -> dict:
+    rate = work / seconds / (1e9 if unit == "GB/s" else 1e12)
+    line = {"op": name, "us": seconds * 1e6, "achieved": rate, "unit": unit, "peak": peak, "frac": rate / peak}
+    line.update(extra)
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def bench_rmsnorm(iters: int) -> None:
+    pk = _peaks()
+    M, d = 16384, 1024
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(M, d, device="cuda", generator=g).half()
+    r = torch.randn(M, d, device="cuda", generator=g).half()
+    gamma = torch.ones(d, device="cuda")
+    y, s = torch.empty_like(x), torch.empty_like(x)
+    rstd = torch.empty(M, device="cuda")
+    t = _time(lambda: ops.rmsnorm_fwd(x, gamma, 1e-5, resid=r, out=y, sum_out=s, rstd=rstd), iters)
+    _emit("rmsnorm_fwd_residual [16384,1024]", t, 4 * M * d * 2 + M * 4 + d * 4, "GB/s", pk["hbm_gbs"])
+    dy = torch.randn(M, d, device="cuda", generator=g).half()
+    dres = torch.randn(M, d, device="cuda", generator=g).half()
+    dx = torch.empty_like(x)
+    dgamma = torch.zeros(d, device="cuda")
+    part = torch.empty(ops._lib.query("jx_rmsnorm_bwd_parts", M) * d, device="cuda")
+    t = _time(lambda: ops.rmsnorm_bwd(dy, s, rstd, gamma, dresid=dres, out=dx, dgamma=dgamma, part=part), iters)
+    _emit("rmsnorm_bwd_residual [16384,1024] (incl. dgamma reduce)", t, 4 * M * d * 2 + M * 4 + d * 4, "GB/s",
+          pk["hbm_gbs"])
+
+
+def bench_ce(iters: int) -> None:
+    pk = _peaks()
+    M, d, V = 16384, 1024, 32000
+    g = torch.Generator(device="cuda").manual_seed(1)
+    h = (torch.randn(M, d, device="cuda", generator=g) * 0.5).half()
+    E = (torch.randn(V, d, device="cuda", generator=g) * 0.02).half()
+    tg = torch.from_numpy(ZipfBatches(V, 16, 1023, seed=2).next_rows().reshape(-1)[:M].copy()).cuda()
+    logits = torch.empty(M, V, device="cuda", dtype=torch.float16)
+    lse = torch.empty(M, device="cuda")
+    row_loss = torch.empty(M, device="cuda")
+    lsc = torch.zeros(3, device="cuda")
+    dh = torch.empty(M, d, device="cuda", dtype=torch.float16)
+    dE = torch.zeros(V, d, device="cuda")
+    grad = torch.tensor([65536.0 / 4], device="cuda")
+
+    def step():
+        ops.gemm_f16(h, E, out=logits)
+        ops.ce_fwd(logits, tg, lse=lse, row_loss=row_loss)
+        ops.ce_loss(row_loss, tg, out=lsc)
+        ops.ce_bwd(logits, tg, lse, grad, lsc[1:2])
+        ops.gemm_f16(logits, E, b_mn_major=True, out=dh)
+        ops.gemm_wgrad(logits, h, dE, False, 1)
+
+    t = _time(step, iters)
+    _emit("fused_ce fwd+bwd h[16384,1024] x E[32000,1024]", t, 3 * 2.0 * M * V * d, "TFLOP/s",
+          pk.get("bf16_tflops_sustained", pk["bf16_tflops"]), flops=3 * 2.0 * M * V * d)
+    t_fwd = _time(lambda: ops.ce_fwd(logits, tg, lse=lse, row_loss=row_loss), iters)
+    t_bwd = _time(lambda: ops.ce_bwd(logits, tg, lse, grad, lsc[1:2]), iters)
+    _emit("ce_softmax_substeps (fwd read + bwd read/write of fp16 logits)", t_fwd + t_bwd, 3 * M * V * 2, "GB/s",
+          pk["hbm_gbs"], fwd_us=t_fwd * 1e6, bwd_us=t_bwd * 1e6, unfused_bytes=2 * M * V * 2)
+
+
+def bench_adamw(iters: int) -> None:
+    pk = _peaks()
+    n = 200_000_000
+    g = torch.Generator(device="cuda").manual_seed(3)
+    p = torch.randn(n, device="cuda", generator=g) * 0.02
+    grad = (torch.randn(n, device="cuda", generator=g) * 1e-3).half()
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    p16 = None
+    inv = torch.tensor([1.0 / 1024], device="cuda")
+    parts = ops.grad_stats_parts(n)
+    partial = torch.empty(parts, device="cuda")
+    found = torch.zeros(1, device="cuda")
+    fin = torch.empty(2, device="cuda")
+    state = torch.zeros(4, device="cuda")
+
+    def step():
+        found.zero_()
+        ops.grad_stats(grad, inv, partial, found)
+        ops.grad_finalize(partial, parts, 1.0, fin)
+        ops.adamw_step(p, grad, m, v, p16, inv, fin[1:2], found, state, 3e-4, 0.9, 0.95, 1e-5, 0.1)
+
+    t = _time(step, iters)
+    _emit("unscale+norm+clip+adamw 200M fp32 params, fp16 grads", t, 28.0 * n, "GB/s", pk["hbm_gbs"],
+          bytes_per_param=28)
+    idx = torch.randperm(n, device="cuda", generator=g)[: n // 100]
+    grad_inf = grad.clone()
+    grad_inf[idx] = float("inf")
+    p0 = p.clone()
+
+    def flagged():
+        found.zero_()
+        ops.grad_stats(grad_inf, inv, partial, found)
+        ops.grad_finalize(partial, parts, 1.0, fin)
+        ops.adamw_step(p, grad_inf, m, v, p16, inv, fin[1:2], found, state, 3e-4, 0.9, 0.95, 1e-5, 0.1)
+
+    t = _time(flagged, iters)
+    torch.cuda.synchronize()
+    skipped = bool(torch.equal(p, p0)) and float(found) == 1.0
+    _emit("flagged step (1% +inf): stats pass only, update skipped on the device", t, 2.0 * n, "GB/s",
+          pk["hbm_gbs"], bytes_per_param=2, update_skipped=skipped)
+
+
+def bench_gemm(iters: int) -> None:
+    pk = _peaks()
+    from .model import rope_tables
+    M, d, F, V = 16384, 1024, 2816, 32000
+    hh = lambda *s: (torch.randn(*s, device="cuda") * 0.5).half()  # noqa: E731
+    x, wqkv, wo, wgu, wd, E = hh(M, d), hh(3 * d, d), hh(d, d), hh(2 * F, d), hh(d, F), hh(V, d)
+    cos, sin = rope_tables(1024, 64, 10000.0, "cuda")
+    qkv = torch.empty(M, 3 * d, device="cuda", dtype=torch.half)
+    gt, up, act = (torch.empty(M, F, device="cuda", dtype=torch.half) for _ in range(3))
+    out = torch.empty(M, d, device="cuda", dtype=torch.half)
+    dgu = torch.empty(M, 2 * F, device="cuda", dtype=torch.half)
+    logits = torch.empty(M, V, device="cuda", dtype=torch.half)
+    G = torch.zeros(2 * F, d, device="cuda")
+    GV = torch.zeros(V, d, device="cuda")
+    ws = torch.empty(64 << 20, device="cuda")
+    peak = pk.get("bf16_tflops", 1590.0)
+    cases = [
+        ("qkv+rope [16384x3072x1024]", 2 * M * 3 * d * d, lambda: ops.gemm_qkv_rope(x, wqkv, d, cos, sin, 1024, 64, out=qkv)),
+        ("o_proj+residual [16384x1024x1024]", 2 * M * d * d, lambda: ops.gemm_f16(x, wo, resid=x, out=out)),
+        ("gate|up+swiglu [16384x5632x1024]", 2 * M * 2 * F * d, lambda: ops.gemm_swiglu_fwd(x, wgu, F, gate=gt, up=up, act=act)),
+        ("down+residual [16384x1024x2816]", 2 * M * d * F, lambda: ops.gemm_f16(act, wd, resid=x, out=out)),
+        ("lm_head [16384x32000x1024]", 2 * M * V * d, lambda: ops.gemm_f16(x, E, out=logits)),
+        ("down dgrad+swiglu bwd [16384x2816x1024]", 2 * M * F * d, lambda: ops.gemm_swiglu_bwd(x, wd, gt, up, out=dgu)),
+        ("gate|up dgrad [16384x1024x5632]", 2 * M * 2 * F * d, lambda: ops.gemm_f16(dgu, wgu, b_mn_major=True, out=out)),
+        ("head dgrad [16384x1024x32000]", 2 * M * V * d, lambda: ops.gemm_f16(logits, E, b_mn_major=True, out=out)),
+        ("gate|up wgrad [5632x1024, 16384 tokens]", 2 * M * 2 * F * d, lambda: ops.gemm_wgrad(dgu, x, G, True, 3, ws)),
+        ("head wgrad [32000x1024, 16384 tokens]", 2 * M * V * d, lambda: ops.gemm_wgrad(logits, x, GV, True, 1, ws)),
+    ]
+    for name, fl, fn in cases:
+        _emit("gemm " + name, _time(fn, iters), fl, "TFLOP/s", peak, peak_kind="bf16_tflops (burst)")
+
+
+def bench_attn(iters: int) -> None:
+    pk = _peaks()
+    for B, T in ((16, 1024), (4, 4096)):
+        H, D = 16, 64
+        qkv = (torch.randn(B * T, 3 * H * D, device="cuda") * 0.5).half()
+        o, lse = ops.attn_fwd(qkv, B, T, H, D)
+        do = torch.randn_like(o)
+        ws = torch.empty(ops.attn_bwd_workspace_bytes(B, T, H, D) // 4 + 4, device="cuda")
+        dqkv = torch.empty_like(qkv)
+        fl = 2.0 * B * H * T * T * D  # causal forward: two T x T x D products, half of them
+        _emit(f"attn_fwd causal B{B} T{T} H16 D64", _time(lambda: ops.attn_fwd(qkv, B, T, H, D, out=o, lse=lse), iters),
+              fl, "TFLOP/s", pk.get("bf16_tflops", 1590.0))
+        _emit(f"attn_bwd causal B{B} T{T} H16 D64", _time(lambda: ops.attn_bwd(qkv, o, do, lse, B, T, H, D, out=dqkv,
+                                                                              workspace=ws), iters),
+              2.5 * fl, "TFLOP/s", pk.get("bf16_tflops", 1590.0))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--op", default="all", choices=("all", "rmsnorm", "ce", "adamw", "gemm", "attn"))
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    for name, fn in (("rmsnorm", bench_rmsnorm), ("ce", bench_ce), ("adamw", bench_adamw), ("gemm", bench_gemm),
+                     ("attn", bench_attn)):
+        if a.op in ("all", name):
+            fn(a.iters)
+            torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()

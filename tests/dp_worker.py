@@ -1,0 +1,81 @@
+"""Worker for tests/test_dp_gpu.py, launched with torch.distributed.run (one rank per GPU).
+
+Each rank computes the decoder's gradients on its own Zipf micro-batch with the
+bucketed NCCL reducer averaging them during backward; rank 0 then recomputes
+the same update as one process accumulating every rank's micro-batch with
+loss / world_size (the data-parallel oracle) and writes the comparison."""
+import json
+import os
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+from midstream_llm_b200 import AdamW, GradScaler, JishuiForCausalLM, causal_lm_loss, train_update  # noqa: E402
+from midstream_llm_b200.config import ModelConfig  # noqa: E402
+from midstream_llm_b200.data import ZipfBatches  # noqa: E402
+from midstream_llm_b200.distributed import (GradReducer, LaunchEnvironment, build_runtime_plan,  # noqa: E402
+                                            initialize_runtime)
+
+CFG = ModelConfig(name="dp", vocab_size=4096, hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                  num_key_value_heads=4, head_dim=64, intermediate_size=688, norm_type="rmsnorm", norm_bias=False,
+                  max_position_embeddings=1024, gradient_checkpointing=False)
+
+
+def model_on(dev):
+    torch.manual_seed(0)
+    m = JishuiForCausalLM(CFG)
+    gen = torch.Generator().manual_seed(0)
+    with torch.no_grad():
+        for _, p in m.named_parameters():
+            p.copy_(torch.randn(p.shape, generator=gen) * 0.02 if p.dim() == 2 else torch.ones(p.shape))
+    return m.to(dev)
+
+
+def batch(rank, dev):
+    rows = torch.from_numpy(ZipfBatches(CFG.vocab_size, 2, 256, seed=100 + rank).next_rows()).to(dev)
+    return rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
+
+
+def main():
+    env = LaunchEnvironment.from_environ()
+    ctx = initialize_runtime(build_runtime_plan("cuda", env), timeout_s=120)
+    dev, world, rank = ctx.torch_device, env.world_size, env.rank
+    scale = 1024.0
+    m = model_on(dev)
+    m.grad_reducer = GradReducer(bucket_bytes=1 << 20)
+    x, y = batch(rank, dev)
+    (causal_lm_loss(m, x, y) * scale).backward()
+    torch.cuda.synchronize()
+    dp_grads = {n: p.grad.detach().clone() for n, p in m.named_parameters()}
+    # one DP optimizer update through the public API, identical on every rank afterwards
+    opt = AdamW(m.parameters(), lr=1e-3, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1)
+    scaler = GradScaler("cuda", init_scale=scale)
+    r = train_update(m, opt, scaler, lambda: [(x, y)], 1, 1.0, 1e-3)
+    flat = torch.cat([p.detach().reshape(-1) for p in m.parameters()])
+    gathered = [torch.empty_like(flat) for _ in range(world)]
+    dist.all_gather(gathered, flat)
+    params_agree = all(torch.equal(g, gathered[0]) for g in gathered)
+    if rank == 0:
+        ref = model_on(dev)
+        for rr in range(world):
+            xr, yr = batch(rr, dev)
+            (causal_lm_loss(ref, xr, yr) * (scale / world)).backward()
+        torch.cuda.synchronize()
+        errs = {}
+        for n, p in ref.named_parameters():
+            a, b = dp_grads[n].double(), p.grad.double()
+            errs[n] = float((a - b).norm() / b.norm().clamp_min(1e-30))
+        out = {"world": world, "max_rel_err": max(errs.values()), "errs": errs, "params_agree": params_agree,
+               "attempts": r["attempts"], "buckets": len(m.grad_reducer.launched)}
+        Path(os.environ["DP_TEST_OUT"]).write_text(json.dumps(out))
+    dist.barrier()
+    ctx.close()
+
+
+if __name__ == "__main__":
+    main()
