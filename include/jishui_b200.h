@@ -73,6 +73,22 @@ int jx_rmsnorm_bwd(const void* dy, const void* x, const float* rstd, const float
 /* dgamma (+)= sum over parts (accumulate != 0 adds to the existing value). */
 int jx_rmsnorm_dgamma_reduce(const float* dgamma_part, int nparts, int cols, float* dgamma, int accumulate,
                              jx_stream_t stream);
+/* RMSNorm backward that allocates nothing and needs no scratch from the caller:
+ * for callers that cannot allocate device memory (a runtime bound through this
+ * C ABI without a device allocator of its own, or one held to a fixed memory
+ * budget that must not call cudaMalloc/cudaFree, which can synchronise the
+ * device). Same results as jx_rmsnorm_bwd followed by jx_rmsnorm_dgamma_reduce
+ * into `dgamma` (accumulate != 0 adds to it). The dgamma partials live in a
+ * fixed device array of 296 x 1024 floats (1.16 MiB) inside the library, held
+ * on every GPU that loads it until the process exits; cols above 1024 are
+ * rejected with JX_ERR_INVALID. The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress with the device current), so
+ * make a first call on each device before any stream capture. All calls share
+ * the one array: calls that overlap on the GPU (e.g. on two streams at once)
+ * race; nothing from an earlier call is read, so no clearing is needed.
+ * This entry point has no counterpart in the reference project. */
+int jx_rmsnorm_bwd_noalloc(const void* dy, const void* x, const float* rstd, const float* gamma, const void* dresid,
+                           void* dx, float* dgamma, int accumulate, int64_t rows, int cols, jx_stream_t stream);
 
 /* ---- Embedding (model_torch.py:89-93): out[t] = table16[ids[t]] ----
  * Ids outside [0, vocab) produce zero rows and set the device status word. */

@@ -10,6 +10,8 @@
 // of `cols` fp16 values is read once with coalesced 16-byte loads and kept in
 // registers. HBM traffic per row: fwd 2*cols*2 bytes (+2*cols*2 with the
 // residual), bwd 3*cols*2 bytes (+cols*2 with the residual gradient).
+#include <mutex>
+
 #include "jx_common.cuh"
 #include "jx_host.h"
 
@@ -300,5 +302,90 @@ extern "C" int jx_rmsnorm_dgamma_reduce(const float* dgamma_part, int nparts, in
   dgamma_reduce_kernel<<<(cols + 31) / 32, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       dgamma_part, nparts, cols, dgamma, accumulate);
   JX_CHECK_LAUNCH("jx_rmsnorm_dgamma_reduce");
+  return JX_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free RMSNorm backward.
+//
+// Some callers cannot allocate device memory at all: a host runtime that binds
+// this library through the C ABI without a device allocator of its own, or one
+// that runs under a fixed, pre-reserved memory budget and must not call
+// cudaMalloc / cudaFree (which can synchronise the whole device and stall other
+// streams). jx_rmsnorm_bwd needs a caller-provided scratch buffer for the
+// per-block dgamma partials; this variant keeps that scratch in a fixed
+// file-scope device array instead, so the caller passes only inputs and
+// outputs. The array holds kNoAllocMaxParts x kNoAllocMaxCols floats
+// (296 x 1024 x 4 B = 1.16 MiB) and stays resident on every GPU that loads the
+// library until the process exits.
+// ---------------------------------------------------------------------------
+namespace jx {
+namespace rms {
+
+constexpr int kNoAllocMaxCols = 1024;
+constexpr int kNoAllocMaxParts = kMaxParts;
+
+static __device__ __align__(256) float g_noalloc_dgamma_part[kNoAllocMaxParts * kNoAllocMaxCols];
+
+// Device address of g_noalloc_dgamma_part on each device, looked up once per
+// device (with that device current) by the first call made on it.
+static float* g_noalloc_ptr[64];
+static std::mutex g_noalloc_mu;
+
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  JX_CUDA_TRY(cudaGetDevice(&dev), "jx_rmsnorm_bwd_noalloc: cudaGetDevice");
+  JX_CHECK_ARG(dev >= 0 && dev < 64, "jx_rmsnorm_bwd_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    JX_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_dgamma_part), "jx_rmsnorm_bwd_noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return JX_OK;
+}
+
+}  // namespace rms
+}  // namespace jx
+
+extern "C" int jx_rmsnorm_bwd_noalloc(const void* dy, const void* x, const float* rstd, const float* gamma,
+                                      const void* dresid, void* dx, float* dgamma, int accumulate, int64_t rows,
+                                      int cols, jx_stream_t stream) {
+  JX_CHECK_ARG(dy && x && rstd && gamma && dx && dgamma, "jx_rmsnorm_bwd_noalloc: NULL argument");
+  JX_CHECK_ARG(rows > 0 && cols > 0 && cols % 8 == 0, "jx_rmsnorm_bwd_noalloc: cols must be a positive multiple of 8");
+  JX_CHECK_ARG(cols <= kNoAllocMaxCols,
+               "jx_rmsnorm_bwd_noalloc: cols %d exceeds the built-in scratch limit of %d columns; use jx_rmsnorm_bwd "
+               "with a caller-provided scratch buffer",
+               cols, kNoAllocMaxCols);
+  JX_CHECK_ARG(aligned16(dy) && aligned16(x) && aligned16(dx) && aligned16(gamma) && (!dresid || aligned16(dresid)),
+               "jx_rmsnorm_bwd_noalloc: buffers must be 16-byte aligned");
+  float* part = nullptr;
+  const int rc = noalloc_scratch(&part);
+  if (rc != JX_OK) return rc;
+  const int nv = pick_nv(cols);
+  const int grid = jx_rmsnorm_bwd_parts(rows);  // <= kNoAllocMaxParts
+  const size_t smem = (size_t)kWarps * cols * sizeof(float);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __half* dyh = static_cast<const __half*>(dy);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* drh = static_cast<const __half*>(dresid);
+  __half* dxh = static_cast<__half*>(dx);
+  // Every block overwrites its own row of partials and the reduction reads only
+  // those rows, so nothing left in the array by an earlier call is ever read.
+  switch (nv) {
+#define X(N)                                                                                                    \
+  case N:                                                                                                       \
+    rmsnorm_bwd_kernel<N><<<grid, kWarps * 32, smem, s>>>(dyh, xh, rstd, gamma, drh, dxh, part, rows, cols); \
+    break;
+    X(1) X(2) X(3) X(4)
+#undef X
+    default:
+      jx::set_error("jx_rmsnorm_bwd_noalloc: unsupported cols %d", cols);
+      return JX_ERR_UNSUPPORTED;
+  }
+  JX_CHECK_LAUNCH("jx_rmsnorm_bwd_noalloc");
+  dgamma_reduce_kernel<<<(cols + 31) / 32, 256, 0, s>>>(part, grid, cols, dgamma, accumulate);
+  JX_CHECK_LAUNCH("jx_rmsnorm_bwd_noalloc: reduce");
   return JX_OK;
 }
