@@ -12,10 +12,12 @@
 //   warp 1     TMEM allocator + MMA issuer, ping-ponging the two tiles:
 //                S_w = Q_w K_j^T (M 128, N 128, K 64) -> TMEM, O_w = P_w V_j (M 128, N 64, K 128),
 //   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B (one query row per
-//              thread): row max over the TMEM S row, fold the previous O_w into
-//              the fp32 output registers with the running rescale, P_w (fp16)
-//              into 128B-swizzled shared memory (the K-major A operand of P V).
-// While one warpgroup runs its softmax the tensor core works on the other's tile.
+//              thread): the S row in registers (one TMEM round trip), row max,
+//              P_w (fp16) into 128B-swizzled shared memory (the K-major A operand
+//              of P V); O_w accumulates in TMEM across key tiles and is rescaled
+//              there only when the row max grows by more than 2^8.
+// S of the next key tile is computed while the softmax of this one runs, and
+// while one warpgroup runs its softmax the tensor core works on the other's tile.
 // q/k/v are read in place from the fused projection output [B*T, 3*H*64] by
 // one TMA descriptor; O is written token-major [B*T, H*64].
 #include "jx_common.cuh"
@@ -156,24 +158,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t a = smem_desc_sw128(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
           // V: [128 keys x 64 hd] read MN-major (hd contiguous), 16 keys = two 8-row groups.
           const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
-          umma_f16(tmem + w * 256 + 128, a, bdesc, idesc_o, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + w * 256 + 128, a, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);  // O accumulates in TMEM
         }
         umma_commit(&bars->p_empty[w]);
         return true;
       };
       if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
       for (int j = 0; j < nkv[1] && ok; ++j) {
+        // S of the next key tile goes ahead of this tile's P V: the softmax has already
+        // moved S_j into registers, so the tensor core computes S_{j+1} while it runs.
         if (j < nkv[0]) {
-          if (!issue_pv(0, j)) break;
           if (j + 1 < nkv[0] && !issue_s(0, j + 1)) break;
+          if (!issue_pv(0, j)) break;
         }
+        if (j + 1 < nkv[1] && !issue_s(1, j + 1)) break;
         if (!issue_pv(1, j)) break;
         umma_commit(&bars->kv_empty[j % KV_STAGES]);
-        if (j + 1 < nkv[1] && !issue_s(1, j + 1)) break;
       }
     }
   } else {
     // Softmax: warpgroup w (0: warps 2-5, 1: warps 6-9); thread owns query row r of its tile.
+    // The output accumulates in TMEM; it is rescaled there only when a row's running
+    // max grows by more than 2^8, otherwise P is formed against the stale max (P <= 256).
     const int w = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -181,121 +187,114 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = qt * BQ + r;  // position in the sequence
     const int n = nkv[w];
     const uint32_t lane_base = tmem + w * 256 + (static_cast<uint32_t>(quarter * 32) << 16);
+    constexpr float kRescaleThreshold = 8.0f;  // log2 units
     float m = -INFINITY, l = 0.f;
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
     bool ok = true;
     for (int j = 0; j < n && ok; ++j) {
       if (!wait(&bars->s_full[w], j & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
       tc_fence_after();
+      uint32_t sr[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) tmem_ld32(lane_base + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->s_free[w]);  // S is in registers; the next S may overwrite it
       const bool diag = (j == n - 1);
-      // pass 1: row max over the 128 raw scores (only the diagonal tile is masked)
-      float mx = -INFINITY;
+      const int lim = diag ? q - j * BKV : BKV;  // columns <= lim are visible
+      // row max with 8 independent partial maxima (short dependency chains)
+      float mp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
       if (!diag) {
 #pragma unroll
-        for (int c = 0; c < BKV / 32; ++c) {
-          uint32_t sr[32];
-          tmem_ld32(lane_base + c * 32, sr);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(sr[i]), __uint_as_float(sr[i + 1])));
-        }
+        for (int i = 0; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[i]));
       } else {
-        const int lim = q - j * BKV;  // keys of this tile at column index <= lim are visible
 #pragma unroll
-        for (int c = 0; c < BKV / 32; ++c) {
-          uint32_t sr[32];
-          tmem_ld32(lane_base + c * 32, sr);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, (c * 32 + i <= lim) ? __uint_as_float(sr[i]) : -INFINITY);
-        }
+        for (int i = 0; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], i <= lim ? __uint_as_float(sr[i]) : -INFINITY);
       }
-      const float m_new = fmaxf(m, mx * scale_log2);
-      const float alpha = ex2(m - m_new);
-      m = m_new;
-      // fold O_{j-1} (scale m_{j-1}) and move to scale m_j; P buffer is then free
-      if (j > 0) {
-        if (!wait(&bars->p_empty[w], (j - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      const float m_cand = mx * scale_log2;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m = m_cand;
+      } else if (m_cand > m + kRescaleThreshold) {
+        alpha = ex2(m - m_cand);
+        m = m_cand;
+        rescale = true;
+      }
+      // P V of the previous tile must be done before P is overwritten or O is rescaled.
+      if (j > 0 && !wait(&bars->p_empty[w], (j - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      // P = exp2(s*scale - m) into the swizzled K-major layout (row r, 16 chunks of 8 keys);
+      // 8 partial row sums.
+      float sp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sp[u] = 0.f;
+      const float neg_m = -m;
+      uint8_t* prow = sP + w * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint32_t wv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i0 = c * 8 + 2 * e;
+          float p0 = ex2(fmaf(__uint_as_float(sr[i0]), scale_log2, neg_m));
+          float p1 = ex2(fmaf(__uint_as_float(sr[i0 + 1]), scale_log2, neg_m));
+          if (diag) {
+            if (i0 > lim) p0 = 0.f;
+            if (i0 + 1 > lim) p1 = 0.f;
+          }
+          sp[(2 * e) & 7] += p0;
+          sp[(2 * e + 1) & 7] += p1;
+          __half2 hp = __floats2half2_rn(p0, p1);
+          wv[e] = *reinterpret_cast<uint32_t*>(&hp);
+        }
+        const int half = c >> 3, ch = c & 7;
+        *reinterpret_cast<uint4*>(prow + half * 16384 + ((ch ^ (r & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      }
+      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+      // Rare: bring the TMEM output to the new max (after P, when the S registers are free).
+      if (__any_sync(0xffffffffu, rescale)) {
         tc_fence_after();
-        uint32_t orr[32];
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
+          uint32_t orr[32];
           tmem_ld32(lane_base + 128 + half * 32, orr);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[half * 32 + i] = (o[half * 32 + i] + __uint_as_float(orr[i])) * alpha;
+          for (int i = 0; i < 32; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+          tmem_st32(lane_base + 128 + half * 32, orr);
         }
-      }
-      // pass 2: P = exp2(s*scale - m) into the swizzled K-major layout (row r, 16 chunks of 8 keys)
-      float sum = 0.f;
-      const float neg_m = -m_new;
-      const int lim = diag ? q - j * BKV : BKV;
-      uint8_t* prow = sP + w * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-      for (int c4 = 0; c4 < BKV / 32; ++c4) {
-        uint32_t sr[32];
-        tmem_ld32(lane_base + c4 * 32, sr);
-        tmem_ld_wait();
-        float pv[32];
-        if (!diag) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pv[i] = ex2(fmaf(__uint_as_float(sr[i]), scale_log2, neg_m));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            pv[i] = (c4 * 32 + i <= lim) ? ex2(fmaf(__uint_as_float(sr[i]), scale_log2, neg_m)) : 0.f;
-        }
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t wv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = pv[cc * 8 + 2 * e], p1 = pv[cc * 8 + 2 * e + 1];
-            sum += p0 + p1;
-            __half2 hp = __floats2half2_rn(p0, p1);
-            wv[e] = *reinterpret_cast<uint32_t*>(&hp);
-          }
-          const int c = c4 * 4 + cc;  // 16-byte chunk index, 0..15
-          const int half = c >> 3, ch = c & 7;
-          *reinterpret_cast<uint4*>(prow + half * 16384 + ((ch ^ (r & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-        }
+        tmem_st_wait();
       }
       l = l * alpha + sum;
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars->s_free[w]);
-        mbar_arrive(&bars->p_full[w]);
-      }
+      if (lane == 0) mbar_arrive(&bars->p_full[w]);
     }
-    if (ok) {
-      // last P V
-      if (!wait(&bars->p_empty[w], (n - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
-    }
+    if (ok && !wait(&bars->p_empty[w], (n - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
     if (ok) {
       tc_fence_after();
-      uint32_t orr[32];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(lane_base + 128 + half * 32, orr);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[half * 32 + i] += __uint_as_float(orr[i]);
-      }
       const float inv = 1.f / l;
       __half* dst = out + (int64_t)(row_base + q) * d + h * D;
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        uint32_t wv[4];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t orr[32];
+        tmem_ld32(lane_base + 128 + half * 32, orr);
+        tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          __half2 hv = __floats2half2_rn(o[c * 8 + 2 * e] * inv, o[c * 8 + 2 * e + 1] * inv);
-          wv[e] = *reinterpret_cast<uint32_t*>(&hv);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __half2 hv = __floats2half2_rn(__uint_as_float(orr[c * 8 + 2 * e]) * inv,
+                                           __uint_as_float(orr[c * 8 + 2 * e + 1]) * inv);
+            wv[e] = *reinterpret_cast<uint32_t*>(&hv);
+          }
+          *reinterpret_cast<uint4*>(dst + half * 32 + c * 8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
-        *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
       }
       lse[((int64_t)b * H + h) * T + q] = (m + __log2f(l)) * 0.69314718055994530942f;
     }
@@ -436,10 +435,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       const uint32_t pt_addr = smem_u32(sPt), st_addr = smem_u32(sSt);
       bool ok = wait(&bars->kv_full, 0, abort_flag, status, kFaMma);
-      for (int t = 0; t < ntiles && ok; ++t) {
+      // S^T = K Q_t^T and dP^T = V dO_t^T into TMEM [0,256) once the softmax has moved the
+      // previous tile's scores into registers.
+      auto issue_sdp = [&](int t) -> bool {
         const int s = t & 1;
-        if (!wait(&bars->q_full[s], (t >> 1) & 1, abort_flag, status, kFaMma)) break;
-        if (!wait(&bars->sdp_free, (t & 1) ^ 1, abort_flag, status, kFaMma)) break;
+        if (!wait(&bars->q_full[s], (t >> 1) & 1, abort_flag, status, kFaMma)) return false;
+        if (!wait(&bars->sdp_free, (t & 1) ^ 1, abort_flag, status, kFaMma)) return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), o_addr = smem_u32(sO + s * kTileBytes);
 #pragma unroll
@@ -450,6 +451,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                    smem_desc_sw128(o_addr + kk * 32, 16, 1024), id_sq, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->sdp_full);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int t = 0; t < ntiles && ok; ++t) {
+        const int s = t & 1;
+        // The next tile's scores are computed while the softmax of this tile runs.
+        if (t + 1 < ntiles && !issue_sdp(t + 1)) break;
+        const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), o_addr = smem_u32(sO + s * kTileBytes);
         if (!wait(&bars->p_full, t & 1, abort_flag, status, kFaMma)) break;
         if (!wait(&bars->dq_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, status, kFaMma)) break;
         tc_fence_after();
