@@ -129,6 +129,11 @@ int jx_gemm_swiglu_bwd(const void* dY, int64_t lddy, const void* Wd, int M, int 
  * Linear's weight gradient is. `splits` > 1 splits the T reduction across
  * CTAs; it needs `workspace` of jx_gemm_wgrad_workspace_bytes(N, K, splits). */
 int64_t jx_gemm_wgrad_workspace_bytes(int N, int K, int splits);
+/* Kernel choice for all GEMM entry points: 0 (default) runs the 2-SM
+ * kernel (a CTA pair per 256 x 256 tile, tcgen05 cta_group::2) whenever M
+ * spans at least two 128-row blocks and the 1-SM kernel otherwise; 1 forces
+ * the 1-SM kernel, 2 the 2-SM kernel. Process-wide; results are identical. */
+int jx_gemm_set_mode(int mode);
 int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_t ldx, int T, int N, int K, float* G,
                   int64_t ldg, int accumulate, int splits, void* workspace, jx_stream_t stream);
 

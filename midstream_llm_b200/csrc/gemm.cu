@@ -559,6 +559,248 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M 256, N 256, K 16). CTA rank r holds rows
+// [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the B tile
+// (half of N) in its own shared memory; the pair of tensor cores exchanges the
+// B halves, and each CTA's TMEM receives its 128 rows x all 256 columns, which
+// its own epilogue warps drain exactly as in the 1-SM kernel. Per k-block each
+// SM therefore stages 32 KiB instead of 48 KiB, which buys a 6-stage ring.
+// Protocol (one leader, CTA rank 0):
+//   both producers   wait their own `empty` slot, TMA (cta_group::2 form, no
+//                    multicast) into their own smem, completing on the leader's
+//                    `full` barrier; only the leader arms it with the pair's bytes,
+//   leader MMA       waits `full`, issues the pair MMA, commits `empty` and
+//                    `acc_full` to both CTAs (commit multicast),
+//   both epilogues   drain their TMEM half and arrive on the leader's `acc_empty`.
+// ---------------------------------------------------------------------------
+constexpr int STAGES2 = 6;
+constexpr uint32_t kAHalf = 128 * BK * 2;  // 16 KiB
+constexpr uint32_t kBHalf = 128 * BK * 2;  // 16 KiB
+constexpr uint32_t kStage2Bytes = kAHalf + kBHalf;
+constexpr size_t kSmem2Bytes = 1024 + STAGES2 * kStage2Bytes + kEpiWarps * kStageOutBytes + 256;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t smem_dst, const CUtensorMap* map, uint32_t leader_bar, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void umma2_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the barrier at this shared offset in both CTAs of the pair once the issued MMAs complete.
+__device__ __forceinline__ void umma2_commit_both(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tile_coords2(const Params& p, int t, int& mb2, int& nb, int& s) {
+  const int tiles_m2 = (p.tiles_m + 1) / 2;
+  const int per_split = tiles_m2 * p.tiles_n;
+  s = t / per_split;
+  const int tt = t - s * per_split;
+  constexpr int GM = 8;  // 8 pair-rows (2048 rows of A) share each sweep over N
+  const int group_span = GM * p.tiles_n;
+  const int g = tt / group_span;
+  const int r = tt - g * group_span;
+  const int rows = min(GM, tiles_m2 - g * GM);
+  mb2 = g * GM + r % rows;
+  nb = r / rows;
+}
+
+template <int EPI, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmC0, const __grid_constant__ CUtensorMap tmC1,
+                 const __grid_constant__ CUtensorMap tmC2, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES2 * kAHalf;
+  uint8_t* sOut = smem + STAGES2 * kStage2Bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kEpiWarps * kStageOutBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES2;
+  uint64_t* acc_full = bars + 2 * STAGES2;
+  uint64_t* acc_empty = bars + 2 * STAGES2 + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = (rank == 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(&full[s], 1);   // leader's producer arms it; both CTAs' TMA bytes complete it
+      mbar_init(&empty[s], 1);  // the leader's MMA commit arrives in both CTAs
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * kEpiWarps);  // epilogue warps of both CTAs (used in the leader)
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive / TMA completion
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m2 = (p.tiles_m + 1) / 2;
+  const int num_tiles = tiles_m2 * p.tiles_n * p.splits;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        int mb2, nb, s;
+        tile_coords2(p, t, mb2, nb, s);
+        const int m0 = mb2 * 256 + rank * 128;  // this CTA's A rows
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const uint32_t stage = it % STAGES2;
+          if (!wait_bar(&empty[stage], ((it / STAGES2) & 1u) ^ 1u, abort_flag, p.status, kStatusGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          const uint32_t leader_full = map_to_rank(smem_u32(&full[stage]), 0);
+          if (leader) mbar_expect_tx(&full[stage], 2 * kStage2Bytes);
+          const uint32_t a_dst = smem_u32(smA + stage * kAHalf);
+          const uint32_t b_dst = smem_u32(smB + stage * kBHalf);
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, leader_full, kb * BK, m0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, leader_full, m0, kb * BK);
+            tma_load_2d_pair(a_dst + 8192, &tmA, leader_full, m0 + 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            int brow;
+            if constexpr (EPI == kSwigluF)
+              brow = (rank == 0 ? 0 : p.swiglu_F) + nb * 128;  // CTA 0: gate rows, CTA 1: up rows
+            else
+              brow = nb * BN + rank * 128;
+            tma_load_2d_pair(b_dst, &tmB, leader_full, kb * BK, brow);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              tma_load_2d_pair(b_dst + j * 8192, &tmB, leader_full, nb * BN + rank * 128 + j * 64, kb * BK);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_f16_f32(256, BN, A_MN, B_MN);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++local) {
+        int mb2, nb, s;
+        tile_coords2(p, t, mb2, nb, s);
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        const int acc = local & 1;
+        if (!wait_bar(&acc_empty[acc], ((local >> 1) & 1) ^ 1, abort_flag, p.status, kStatusGemmMmaWait)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const uint32_t stage = it % STAGES2;
+          if (!wait_bar(&full[stage], (it / STAGES2) & 1u, abort_flag, p.status, kStatusGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smA + stage * kAHalf);
+          const uint32_t b_base = smem_u32(smB + stage * kBHalf);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? smem_desc_sw128(a_base + k * 2048, 8192, 1024)
+                                        : smem_desc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_base + k * 2048, 8192, 1024)
+                                        : smem_desc_sw128(b_base + k * 32, 16, 1024);
+            umma2_f16(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma2_commit_both(&empty[stage]);
+        }
+        if (ok) umma2_commit_both(&acc_full[acc]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    Stager st{sOut + (warp - 2) * kStageOutBytes, lane};
+    const OutMaps om{&tmC0, &tmC1, &tmC2};
+    const uint32_t leader_acc_empty0 = map_to_rank(smem_u32(&acc_empty[0]), 0);
+    const uint32_t leader_acc_empty1 = map_to_rank(smem_u32(&acc_empty[1]), 0);
+    int local = 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
+      int mb2, nb, s;
+      tile_coords2(p, t, mb2, nb, s);
+      const int acc = local & 1;
+      if (!wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
+      tc_fence_after();
+      epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb2 * 2 + (int)rank, nb, s);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+}
+
 // Split-K reduction for the weight gradient: G (+)= f32(f16(sum_s ws[s])).
 __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, float* __restrict__ G,
                                     int64_t ldg, int accumulate) {
@@ -627,6 +869,9 @@ bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
 
 namespace gemm {
 
+// 0: choose (2-SM when there are at least two 128-row blocks), 1: force 1-SM, 2: force 2-SM.
+static int g_gemm_mode = 0;
+
 template <int EPI, bool A_MN, bool B_MN>
 static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params p, cudaStream_t stream,
                   const char* name) {
@@ -643,8 +888,9 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
     ok = make_tmap_f16(&ta, A, p.M, p.K, lda, 64, BK);
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for A", name);
   const int b_rows = (EPI == kSwigluF) ? 2 * p.swiglu_F : p.N;
+  const bool two_sm = (g_gemm_mode == 2) || (g_gemm_mode == 0 && p.M > BM);
   if (!B_MN)
-    ok = make_tmap_f16(&tb, B, p.K, b_rows, ldb, BK, (EPI == kSwigluF) ? 128 : BN);
+    ok = make_tmap_f16(&tb, B, p.K, b_rows, ldb, BK, (EPI == kSwigluF || two_sm) ? 128 : BN);
   else
     ok = make_tmap_f16(&tb, B, b_rows, p.K, ldb, 64, BK);
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for B", name);
@@ -671,6 +917,35 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
   p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
   p.status = status_ptr();
 
+  if (two_sm) {
+    static int max_clusters = 0;  // per template instantiation
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmem2Bytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (!max_clusters) {
+      JX_CUDA_TRY(cudaFuncSetAttribute(gemm2_kernel<EPI, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmem2Bytes),
+                  name);
+      cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+      int n = 0;
+      JX_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, gemm2_kernel<EPI, A_MN, B_MN>, &cfg), name);
+      max_clusters = n > 0 ? n : 1;
+    }
+    const int tiles2 = ((p.tiles_m + 1) / 2) * p.tiles_n * p.splits;
+    const int clusters = tiles2 < max_clusters ? tiles2 : max_clusters;
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    JX_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm2_kernel<EPI, A_MN, B_MN>, ta, tb, tc0, tc1, tc2, p), name);
+    JX_CHECK_LAUNCH(name);
+    return JX_OK;
+  }
   static bool attr_set = false;  // per template instantiation
   if (!attr_set) {
     JX_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<EPI, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -799,5 +1074,11 @@ extern "C" int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_
   if (blocks > num_sms() * 8) blocks = num_sms() * 8;
   wgrad_reduce_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(workspace), sp, N, K, G, ldg, accumulate);
   JX_CHECK_LAUNCH("jx_gemm_wgrad: reduce");
+  return JX_OK;
+}
+
+extern "C" int jx_gemm_set_mode(int mode) {
+  JX_CHECK_ARG(mode >= 0 && mode <= 2, "jx_gemm_set_mode: mode must be 0 (auto), 1 (1-SM) or 2 (2-SM)");
+  jx::gemm::g_gemm_mode = mode;
   return JX_OK;
 }

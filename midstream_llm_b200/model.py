@@ -250,17 +250,18 @@ class Workspace:
     extra: dict = field(default_factory=dict)
 
 
-def _wgrad_splits(n: int, k: int, tokens: int = 16384, sms: int = 148) -> int:
-    """Split count for a weight-gradient GEMM with [n, k] output (128x256 tiles)
-    reducing over `tokens`: minimises (waves x per-split main loop) + the split-K
-    partials' HBM round trip, with a per-SM rate of ~7.4 TFLOP/s and 6 TB/s."""
-    tiles = -(-n // 128) * -(-k // 256)
-    tile_us = 2.0 * 128 * 256 * tokens / 7.4e6  # one tile over all tokens, microseconds
+def _wgrad_splits(n: int, k: int, tokens: int = 16384, pairs: int = 74) -> int:
+    """Split count for a weight-gradient GEMM with [n, k] output reducing over
+    `tokens`, for the 2-SM kernel (a CTA pair per 256 x 256 tile, `pairs` pairs
+    resident): minimises (waves x per-split main loop) + the split-K partials'
+    HBM round trip, at ~14.8 TFLOP/s per pair and 6 TB/s."""
+    tiles = -(-n // 256) * -(-k // 256)
+    tile_us = 2.0 * 256 * 256 * tokens / 14.8e6  # one tile over all tokens, microseconds
     best, best_t = 1, None
     for s in range(1, 9):
         if tokens // s < 1024:
             break
-        t = math.ceil(tiles * s / sms) * tile_us / s
+        t = math.ceil(tiles * s / pairs) * tile_us / s
         if s > 1:
             t += (2.0 * s + 2.0) * n * k * 4 / 6e6
         if best_t is None or t < best_t * 0.97:

@@ -20,6 +20,15 @@ def ops():
     return _ops
 
 
+@pytest.fixture(params=[1, 2], ids=["1sm", "2sm"])
+def gemm_mode(request, ops):
+    """Runs a GEMM test once with the 1-SM kernel and once with the 2-SM (CTA pair) kernel."""
+    from midstream_llm_b200 import _lib
+    _lib.call("jx_gemm_set_mode", request.param)
+    yield request.param
+    _lib.call("jx_gemm_set_mode", 0)
+
+
 def _h(*shape, scale=1.0, seed=0):
     g = torch.Generator(device="cuda").manual_seed(seed)
     return (torch.randn(*shape, device="cuda", generator=g) * scale).half()
@@ -27,7 +36,7 @@ def _h(*shape, scale=1.0, seed=0):
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("M,N,K", [(256, 512, 128), (296, 264, 200), (1024, 3072, 1024)])
-def test_gemm_f16_majors(ops, a_mn, b_mn, M, N, K):
+def test_gemm_f16_majors(ops, gemm_mode, a_mn, b_mn, M, N, K):
     a = _h(M, K, seed=1)
     b = _h(N, K, seed=2)
     ref = a.float() @ b.float().t()
@@ -38,7 +47,7 @@ def test_gemm_f16_majors(ops, a_mn, b_mn, M, N, K):
     assert rel_err(c, ref) < TOL, (a_mn, b_mn, M, N, K, rel_err(c, ref))
 
 
-def test_gemm_resid(ops):
+def test_gemm_resid(ops, gemm_mode):
     M, N, K = 512, 1024, 1024
     a, b, r = _h(M, K, seed=1), _h(N, K, seed=2), _h(M, N, seed=3)
     c = ops.gemm_f16(a, b, resid=r)
@@ -59,7 +68,7 @@ def _rope_ref(x, cos, sin):
     return torch.cat((a * c - b * s, a * s + b * c), dim=-1)
 
 
-def test_gemm_qkv_rope(ops):
+def test_gemm_qkv_rope(ops, gemm_mode):
     B, T, H, hd = 2, 256, 4, 64
     d = H * hd
     x = _h(B * T, d, seed=4)
@@ -73,7 +82,7 @@ def test_gemm_qkv_rope(ops):
     assert rel_err(out, ref) < TOL
 
 
-def test_swiglu_fwd_bwd(ops):
+def test_swiglu_fwd_bwd(ops, gemm_mode):
     M, d, F = 512, 256, 688
     x = _h(M, d, seed=6)
     wgu = _h(2 * F, d, scale=0.05, seed=7)
@@ -95,7 +104,7 @@ def test_swiglu_fwd_bwd(ops):
 
 
 @pytest.mark.parametrize("splits", [1, 4])
-def test_wgrad(ops, splits):
+def test_wgrad(ops, gemm_mode, splits):
     T, N, K = 2048, 1024, 512
     dy, x = _h(T, N, seed=10), _h(T, K, seed=11)
     g = torch.randn(N, K, device="cuda")
