@@ -62,6 +62,19 @@ __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, volatile in
   }
 }
 
+// Warp-wide wait where only lane 0 polls the barrier (all 32 lanes must be active).
+// Used for barriers that publish TMEM contents or free a resource; the other
+// lanes are ordered after lane 0's acquire by __syncwarp, and TMEM reads that
+// follow are ordered by tcgen05.fence::after_thread_sync.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          int code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = wait(bar, parity, abort_flag, status, code) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n && ok; ++j) {
-      if (!wait(&bars->s_full[w], j & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      if (!warp_wait(&bars->s_full[w], j & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
       tc_fence_after();
       uint32_t sr[BKV];
 #pragma unroll
@@ -225,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         rescale = true;
       }
       // P V of the previous tile must be done before P is overwritten or O is rescaled.
-      if (j > 0 && !wait(&bars->p_empty[w], (j - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      if (j > 0 && !warp_wait(&bars->p_empty[w], (j - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
       // P = exp2(s*scale - m) into the swizzled K-major layout (row r, 16 chunks of 8 keys);
       // 8 partial row sums.
       float sp[8];
@@ -274,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[w]);
     }
-    if (ok && !wait(&bars->p_empty[w], (n - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
+    if (ok && !warp_wait(&bars->p_empty[w], (n - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
     if (ok) {
       tc_fence_after();
       const float inv = 1.f / l;
@@ -326,8 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // TMEM lane quarter, each on half of the columns).
 // ---------------------------------------------------------------------------
 constexpr int kBwdThreads = 320;
+constexpr uint32_t kDqStageBytes = 32 * 32 * 4;  // one warp's [32 rows x 32 cols] fp32 dQ block
 constexpr size_t kBwdSmem = 1024 + 2 * kTileBytes /*K,V*/ + 4 * kTileBytes /*Q,dO x2*/ + 2 * kPBytes /*P^T, dS^T*/ +
-                            2 * 2 * BQ * sizeof(float) /*LSE, Delta x2*/ + 512;
+                            8 * kDqStageBytes /*dQ staging*/ + 2 * 2 * BQ * sizeof(float) /*LSE, Delta x2*/ + 512;
 
 struct BwdBars {
   uint64_t kv_full;
@@ -358,6 +372,7 @@ __device__ __forceinline__ void rope_back(float& g1, float& g2, const float* cs,
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_dq,
                        const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq_acc,
                        __half* __restrict__ dqkv, int T, int H, float scale, float scale_log2,
                        const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, int* status) {
@@ -369,7 +384,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sO = sQ + 2 * kTileBytes;         // dO, 2 stages
   uint8_t* sPt = sO + 2 * kTileBytes;        // P^T  [128 keys x 128 queries]
   uint8_t* sSt = sPt + kPBytes;              // dS^T [128 keys x 128 queries]
-  float* sL = reinterpret_cast<float*>(sSt + kPBytes);  // [2][128]
+  uint8_t* sDq = sSt + kPBytes;              // [8 warps][32 x 32] fp32 dQ staging (128B-swizzled)
+  float* sL = reinterpret_cast<float*>(sDq + 8 * kDqStageBytes);  // [2][128]
   float* sD = sL + 2 * BQ;                               // [2][128]
   BwdBars* bars = reinterpret_cast<BwdBars*>(sD + 2 * BQ);
   volatile int* abort_flag = &bars->abort;
@@ -486,7 +502,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int r = quarter * 32 + lane;    // key row (S^T / dP^T / dK / dV) or query row (dQ)
     const int key = kb * BKV + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    // dQ of query tile tp: TMEM lanes are query rows; this warp adds 32 of the 64 columns.
+    // dQ of query tile tp: TMEM lanes are query rows; this warp adds 32 of the 64 columns,
+    // staged in shared memory and added to the fp32 accumulator by one TMA reduce.
+    uint8_t* dq_stage = sDq + (warp - 2) * kDqStageBytes;
     auto drain_dq = [&](int tp) {
       const int buf = tp & 1;
       tc_fence_after();
@@ -495,20 +513,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->dq_free[buf]);
-      float* dst = dq_acc + (int64_t)(row_base + (kb + tp) * BQ + r) * d + h * D + colh * 32;
+      if (lane == 0) {
+        mbar_arrive(&bars->dq_free[buf]);
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // previous reduce has read the staging
+      }
+      __syncwarp();
 #pragma unroll
-      for (int g = 0; g < 8; ++g)
-        atomicAdd(reinterpret_cast<float4*>(dst + g * 4),
-                  make_float4(__uint_as_float(qr[g * 4]), __uint_as_float(qr[g * 4 + 1]),
-                              __uint_as_float(qr[g * 4 + 2]), __uint_as_float(qr[g * 4 + 3])));
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(dq_stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+            make_uint4(qr[c * 4], qr[c * 4 + 1], qr[c * 4 + 2], qr[c * 4 + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile(
+            "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                reinterpret_cast<uint64_t>(&tm_dq)),
+            "r"(smem_u32(dq_stage)), "r"(h * D + colh * 32), "r"(row_base + (kb + tp) * BQ + quarter * 32)
+            : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
     };
     bool ok = true;
     for (int t = 0; t < ntiles && ok; ++t) {
       const int s = t & 1, qi = kb + t;
       const bool diag = (t == 0);
       if (!wait(&bars->q_full[s], (t >> 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
-      if (!wait(&bars->sdp_full, t & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      if (!warp_wait(&bars->sdp_full, t & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
       tc_fence_after();
       const float* Ls = sL + s * BQ;
       const float* Ds = sD + s * BQ;
@@ -549,7 +579,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->sdp_free);
       // The previous tile's MMAs must be done reading P^T / dS^T before they are overwritten.
-      if (t > 0 && !wait(&bars->grads_done, (t - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      if (t > 0 && !warp_wait(&bars->grads_done, (t - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
       uint8_t* prow = sPt + colh * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
       uint8_t* srow = sSt + colh * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
@@ -564,7 +594,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // The previous tile's dQ is complete (grads_done(t-1)); reduce it while this tile's MMAs run.
       if (t > 0) drain_dq(t - 1);
     }
-    if (ok && !wait(&bars->grads_done, (ntiles - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
+    if (ok && !warp_wait(&bars->grads_done, (ntiles - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
     if (ok) drain_dq(ntiles - 1);
     if (ok) {
       // dK (warps with colh 0, scaled, rotated back through RoPE) and dV (colh 1).
@@ -594,6 +624,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // dQ reduces complete
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -701,6 +733,9 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
   CUtensorMap tq, tdo;
   JX_CHECK_ARG(make_tmap_f16(&tq, qkv, 3LL * d, rows, 3LL * d, D, BKV), "jx_attn_bwd: cannot encode TMA descriptor");
   JX_CHECK_ARG(make_tmap_f16(&tdo, dout, d, rows, d, D, BQ), "jx_attn_bwd: cannot encode TMA descriptor");
+  CUtensorMap tdq;
+  JX_CHECK_ARG(make_tmap_f32(&tdq, static_cast<float*>(workspace) + (int64_t)B * H * T, d, rows, d, 32, 32),
+               "jx_attn_bwd: cannot encode TMA descriptor for the dQ accumulator");
   JX_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)rows * d * sizeof(float), s), "jx_attn_bwd: clear dq accumulator");
   jx::attn::launch_delta(static_cast<const __half*>(out), static_cast<const __half*>(dout), delta, B, T, H, s);
   JX_CHECK_LAUNCH("jx_attn_bwd: delta");
@@ -711,7 +746,7 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
     attr_set = true;
   }
   dim3 grid(T / BKV, H, B);
-  attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, lse, delta, dq_acc, static_cast<__half*>(dqkv), T, H,
+  attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, tdq, lse, delta, dq_acc, static_cast<__half*>(dqkv), T, H,
                                                         scale, scale * 1.4426950408889634f, rope_cos, rope_sin,
                                                         status_ptr());
   JX_CHECK_LAUNCH("jx_attn_bwd");

@@ -89,6 +89,17 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
   }
 }
 
+// Warp-wide wait where only lane 0 polls (all 32 lanes active); the accumulator
+// it guards lives in TMEM, read after tcgen05.fence::after_thread_sync.
+__device__ __forceinline__ bool warp_wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                              int code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = wait_bar(bar, parity, abort_flag, status, code) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& mb, int& nb, int& s) {
   const int per_split = p.tiles_m * p.tiles_n;
   s = t / per_split;
@@ -540,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int mb, nb, s;
       tile_coords(p, t, mb, nb, s);
       const int acc = local & 1;
-      if (!wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
+      if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
       epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb, nb, s);
       tc_fence_before();
@@ -782,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int mb2, nb, s;
       tile_coords2(p, t, mb2, nb, s);
       const int acc = local & 1;
-      if (!wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
+      if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
       epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb2 * 2 + (int)rank, nb, s);
       tc_fence_before();
@@ -862,6 +873,20 @@ bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                   uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
