@@ -140,8 +140,12 @@ int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_t ldx, int 
 /* ---- Causal attention (model_torch.py:48, SDPA is_causal=True) ----
  * qkv: f16 [B*T, 3*H*D] rows (q | k | v, head h at column h*D of each part).
  * out: f16 [B*T, H*D]. lse: f32 [B, H, T] (natural-log logsumexp of the scaled scores).
- * D must be 64; T a multiple of 256 (forward) / 128 (backward). */
-int jx_attn_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int D, float scale,
+ * D must be 64; T a multiple of 256 (forward) / 128 (backward).
+ * `workspace` is caller scratch of jx_attn_fwd_workspace_bytes(B, T, H, D) bytes (the
+ * work counter of the persistent kernel, cleared by the call on `stream`); calls that
+ * may run concurrently need separate workspaces. */
+int64_t jx_attn_fwd_workspace_bytes(int B, int T, int H, int D);
+int jx_attn_fwd(const void* qkv, void* out, float* lse, void* workspace, int B, int T, int H, int D, float scale,
                 jx_stream_t stream);
 /* Backward: writes dqkv f16 [B*T, 3*H*D]. `workspace` is caller scratch of
  * jx_attn_bwd_workspace_bytes(B, T, H, D) bytes (the row sums dO.O and an fp32

@@ -6,20 +6,27 @@
 // fp16 operands, fp32 softmax; the forward saves O and the natural-log LSE per
 // row, the backward recomputes the probabilities from them.
 //
-// Forward: one CTA per pair of 128-query tiles (A = 2p, B = 2p+1) of one
-// (head, batch), 320 threads:
-//   warp 0     TMA producer: Q_A, Q_B once, then K_j / V_j (128 keys) into a 3-stage ring,
+// Forward: a persistent kernel, one CTA per SM. A work item is a
+// pair of 128-query tiles (A = 2p, B = 2p+1) of one (head, batch); the CTAs
+// take items from a global counter, heaviest first within chunks of 32
+// (head, batch) pairs, and the loads of the next item overlap the last key
+// tiles and the output of the current one.
+// 320 threads:
+//   warp 0     TMA producer: Q_A, Q_B per item, K_j / V_j (128 keys) into a 4-stage ring,
 //   warp 1     TMEM allocator + MMA issuer, ping-ponging the two tiles:
-//                S_w = Q_w K_j^T (M 128, N 128, K 64) -> TMEM, O_w = P_w V_j (M 128, N 64, K 128),
+//                S_w = Q_w K_j^T (M 128, N 128, K 64, operands in shared memory) -> TMEM,
+//                O_w += P_w V_j  (M 128, N 64, K 128, P_w read from TMEM),
 //   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B (one query row per
 //              thread): the S row in registers (one TMEM round trip), row max,
-//              P_w (fp16) into 128B-swizzled shared memory (the K-major A operand
-//              of P V); O_w accumulates in TMEM across key tiles and is rescaled
-//              there only when the row max grows by more than 2^8.
+//              P_w (fp16 pairs) stored back to TMEM;
+//              O_w accumulates in TMEM across key tiles and is rescaled there only
+//              when the row max grows by more than 2^8.
 // S of the next key tile is computed while the softmax of this one runs, and
 // while one warpgroup runs its softmax the tensor core works on the other's tile.
 // q/k/v are read in place from the fused projection output [B*T, 3*H*64] by
 // one TMA descriptor; O is written token-major [B*T, H*64].
+#include <algorithm>
+
 #include "jx_common.cuh"
 #include "jx_host.h"
 
@@ -29,20 +36,29 @@ namespace fa {
 constexpr int D = 64;
 constexpr int BQ = 128;
 constexpr int BKV = 128;
-constexpr int KV_STAGES = 3;
-constexpr int kThreads = 320;
+constexpr int KV_STAGES = 4;
+constexpr int kFwdThreads = 320;
 constexpr uint32_t kTileBytes = BKV * D * 2;  // 16 KiB (one [128 x 64] fp16 tile)
-constexpr uint32_t kPBytes = BQ * BKV * 2;    // 32 KiB
+constexpr uint32_t kPBytes = BQ * BKV * 2;    // 32 KiB (backward P^T / dS^T staging)
 constexpr uint32_t kTmemCols = 512;
-// smem: Q_A, Q_B | K stages | V stages | P_A, P_B | barriers
-constexpr size_t kSmemBytes = 1024 + 2 * kTileBytes + 2 * KV_STAGES * kTileBytes + 2 * kPBytes + 512;
+// smem: Q_A, Q_B | K stages | V stages | barriers
+constexpr size_t kSmemBytes = 1024 + 2 * kTileBytes + 2 * KV_STAGES * kTileBytes + 512;
+
+constexpr int kItemSlots = 4;
+constexpr int kItemConsumers = 9;  // the MMA thread + 8 softmax warps
+
+struct ItemRing {
+  uint64_t full[kItemSlots], empty[kItemSlots];
+  int idx[kItemSlots];
+};
 
 enum Status : int { kFaProducer = 301, kFaMma = 302, kFaSoftmax = 303 };
 
 struct Bars {
-  uint64_t q_full;
+  uint64_t q_full, q_empty;
   uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
   uint64_t s_full[2], s_free[2], p_full[2], p_empty[2];  // per query tile (A, B)
+  ItemRing items;
   uint32_t tmem_base;
   int abort;
 };
@@ -81,28 +97,92 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// ---------------------------------------------------------------------------
+// Work distribution of the persistent forward. Work items are numbered in
+// chunks of whole (head, batch) pairs; inside a chunk the heaviest items of all
+// its pairs come first (the longest causal rows), then the next lighter, so the
+// CTAs running at the same time share the K/V tiles of one chunk in L2 while
+// each chunk still ends on its lightest items. The producer
+// warp of each CTA takes the next number from a global counter (zeroed on the
+// stream before the launch) and hands it to the MMA and softmax warps through
+// a small ring of slots in shared memory.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ring_init(ItemRing* r) {
+  for (int s = 0; s < kItemSlots; ++s) {
+    mbar_init(&r->full[s], 1);
+    mbar_init(&r->empty[s], kItemConsumers);
+  }
+}
+
+// Producer: publish work number idx as this CTA's n-th item (false if the wait gave up).
+__device__ __forceinline__ bool ring_publish(ItemRing* r, uint32_t n, int idx, volatile int* abort_flag, int* status,
+                                             int code) {
+  const int s = n % kItemSlots;
+  if (!wait(&r->empty[s], ((n / kItemSlots) & 1) ^ 1, abort_flag, status, code)) return false;
+  *reinterpret_cast<volatile int*>(&r->idx[s]) = idx;
+  mbar_arrive(&r->full[s]);  // release: the slot store is visible to the waiting consumers
+  return true;
+}
+
+// Consumer (one thread): the n-th item's work number, or -1 if the wait gave up.
+__device__ __forceinline__ int ring_take(ItemRing* r, uint32_t n, volatile int* abort_flag, int* status, int code) {
+  const int s = n % kItemSlots;
+  if (!wait(&r->full[s], (n / kItemSlots) & 1, abort_flag, status, code)) return -1;
+  const int idx = *reinterpret_cast<volatile int*>(&r->idx[s]);
+  mbar_arrive(&r->empty[s]);
+  return idx;
+}
+
+// Consumer (whole warp): lane 0 takes the slot, the number is broadcast.
+__device__ __forceinline__ int ring_take_warp(ItemRing* r, uint32_t n, volatile int* abort_flag, int* status,
+                                              int code) {
+  int idx = 0;
+  if ((threadIdx.x & 31) == 0) idx = ring_take(r, n, abort_flag, status, code);
+  return __shfl_sync(0xffffffffu, idx, 0);
+}
+
+// Work number -> (chunk of `chunk` pairs, item rank inside the chunk, pair). Pair p is
+// (head p % H, batch p / H). Returns the rank (0 = heaviest) and sets *pair.
+__device__ __forceinline__ int chunked_rank(int idx, int per_pair, int chunk, int pairs, int* pair) {
+  const int ci = idx / (chunk * per_pair);
+  const int first = ci * chunk;
+  const int n = min(chunk, pairs - first);
+  const int local = idx - ci * chunk * per_pair;
+  *pair = first + local % n;
+  return local / n;
+}
+
+constexpr int kFwdChunk = 32;  // (head, batch) pairs per chunk of the forward
+
+struct FwdItem {
+  int pr, h, b;
+};
+
+__device__ __forceinline__ FwdItem fwd_decode(int idx, int npairs, int H, int B) {
+  int pair;
+  const int rank = chunked_rank(idx, npairs, kFwdChunk, H * B, &pair);
+  return FwdItem{npairs - 1 - rank, pair % H, pair / H};
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __half* __restrict__ out, float* __restrict__ lse,
-                       int T, int H, float scale_log2, int* status) {
+                       int* __restrict__ work_counter, int B, int T, int H, float scale_log2, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                         // [2] query tiles
   uint8_t* sK = sQ + 2 * kTileBytes;
   uint8_t* sV = sK + KV_STAGES * kTileBytes;
-  uint8_t* sP = sV + KV_STAGES * kTileBytes;  // [2] P tiles
-  Bars* bars = reinterpret_cast<Bars*>(sP + 2 * kPBytes);
+  Bars* bars = reinterpret_cast<Bars*>(sV + KV_STAGES * kTileBytes);
   volatile int* abort_flag = &bars->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npairs = T / (2 * BQ);
-  const int pr = npairs - 1 - blockIdx.x;  // heaviest pair first
-  const int h = blockIdx.y, b = blockIdx.z;
   const int d = H * D;
-  const int row_base = b * T;
-  const int nkv[2] = {2 * pr + 1, 2 * pr + 2};  // key tiles of query tiles A = 2pr and B = 2pr+1
+  const int total = npairs * H * B;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
@@ -113,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->p_full[w], 4);
       mbar_init(&bars->p_empty[w], 1);
     }
+    ring_init(&bars->items);
     bars->abort = 0;
     fence_barrier_init();
   }
@@ -124,31 +205,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  // TMEM columns of tile w: S at w*256 + [0,128), O at w*256 + [128,192).
+  // TMEM columns of query-tile slot w: S at w*256 + [0,128), P (fp16 pairs) at
+  // w*256 + [128,192), O at w*256 + [192,256).
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp < 2) {
+    if (warp == 0 && lane == 0) {
       tma_prefetch_desc(&tm_qkv);
-      mbar_expect_tx(&bars->q_full, 2 * kTileBytes);
-      tma_load_2d(sQ, &tm_qkv, &bars->q_full, h * D, row_base + (2 * pr) * BQ);
-      tma_load_2d(sQ + kTileBytes, &tm_qkv, &bars->q_full, h * D, row_base + (2 * pr + 1) * BQ);
-      for (int j = 0; j < nkv[1]; ++j) {
-        const int s = j % KV_STAGES;
-        if (!wait(&bars->kv_empty[s], ((j / KV_STAGES) & 1) ^ 1, abort_flag, status, kFaProducer)) break;
-        mbar_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
-        tma_load_2d(sK + s * kTileBytes, &tm_qkv, &bars->kv_full[s], d + h * D, row_base + j * BKV);
-        tma_load_2d(sV + s * kTileBytes, &tm_qkv, &bars->kv_full[s], 2 * d + h * D, row_base + j * BKV);
+      uint32_t kv = 0;
+      for (uint32_t round = 0;; ++round) {
+        const int idx = atomicAdd(work_counter, 1);
+        if (!ring_publish(&bars->items, round, idx, abort_flag, status, kFaProducer) || idx >= total) break;
+        const FwdItem it = fwd_decode(idx, npairs, H, B);
+        const int row_base = it.b * T;
+        // The query tiles are free once the previous item's last S MMAs completed.
+        if (!wait(&bars->q_empty, (round & 1) ^ 1, abort_flag, status, kFaProducer)) break;
+        mbar_expect_tx(&bars->q_full, 2 * kTileBytes);
+        tma_load_2d(sQ, &tm_qkv, &bars->q_full, it.h * D, row_base + (2 * it.pr) * BQ);
+        tma_load_2d(sQ + kTileBytes, &tm_qkv, &bars->q_full, it.h * D, row_base + (2 * it.pr + 1) * BQ);
+        const int n = 2 * it.pr + 2;
+        bool ok = true;
+        for (int j = 0; j < n; ++j, ++kv) {
+          const int s = kv % KV_STAGES;
+          if (!wait(&bars->kv_empty[s], ((kv / KV_STAGES) & 1) ^ 1, abort_flag, status, kFaProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
+          tma_load_2d(sK + s * kTileBytes, &tm_qkv, &bars->kv_full[s], d + it.h * D, row_base + j * BKV);
+          tma_load_2d(sV + s * kTileBytes, &tm_qkv, &bars->kv_full[s], 2 * d + it.h * D, row_base + j * BKV);
+        }
+        if (!ok) break;
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV, false, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
-      bool ok = wait(&bars->q_full, 0, abort_flag, status, kFaMma);
-      auto issue_s = [&](int w, int j) -> bool {
-        const int s = j % KV_STAGES;
-        if (!wait(&bars->kv_full[s], (j / KV_STAGES) & 1, abort_flag, status, kFaMma)) return false;
-        if (!wait(&bars->s_free[w], (j & 1) ^ 1, abort_flag, status, kFaMma)) return false;
+      uint32_t kv = 0;
+      uint32_t ns[2] = {0, 0}, np[2] = {0, 0};  // S tiles issued / P V products issued per slot
+      auto issue_s = [&](int w, uint32_t kvi) -> bool {
+        const int s = kvi % KV_STAGES;
+        if (!wait(&bars->kv_full[s], (kvi / KV_STAGES) & 1, abort_flag, status, kFaMma)) return false;
+        if (!wait(&bars->s_free[w], (ns[w] & 1) ^ 1, abort_flag, status, kFaMma)) return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(sQ + w * kTileBytes);
         const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
@@ -157,36 +253,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16(tmem + w * 256, smem_desc_sw128(q_addr + kk * 32, 16, 1024),
                    smem_desc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(&bars->s_full[w]);
+        ++ns[w];
         return true;
       };
-      auto issue_pv = [&](int w, int j) -> bool {
-        const int s = j % KV_STAGES;
-        if (!wait(&bars->p_full[w], j & 1, abort_flag, status, kFaMma)) return false;
+      auto issue_pv = [&](int w, uint32_t kvi, bool first) -> bool {
+        const int s = kvi % KV_STAGES;
+        if (!wait(&bars->p_full[w], np[w] & 1, abort_flag, status, kFaMma)) return false;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + w * kPBytes);
         const uint32_t v_addr = smem_u32(sV + s * kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          // P: K-major [128 q x 128 keys] as two 64-key halves of 16 KiB each.
-          const uint64_t a = smem_desc_sw128(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          // V: [128 keys x 64 hd] read MN-major (hd contiguous), 16 keys = two 8-row groups.
+          // P from TMEM (16 keys = 8 packed columns per step); V [128 keys x 64 hd] read
+          // MN-major (hd contiguous), 16 keys = two 8-row groups.
           const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
-          umma_f16(tmem + w * 256 + 128, a, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);  // O accumulates in TMEM
+          umma_f16_ts(tmem + w * 256 + 192, tmem + w * 256 + 128 + kk * 8, bdesc, idesc_o,
+                      (!first || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->p_empty[w]);
+        ++np[w];
         return true;
       };
-      if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
-      for (int j = 0; j < nkv[1] && ok; ++j) {
-        // S of the next key tile goes ahead of this tile's P V: the softmax has already
-        // moved S_j into registers, so the tensor core computes S_{j+1} while it runs.
-        if (j < nkv[0]) {
-          if (j + 1 < nkv[0] && !issue_s(0, j + 1)) break;
-          if (!issue_pv(0, j)) break;
+      bool ok = true;
+      for (uint32_t round = 0; ok; ++round) {
+        const int idx = ring_take(&bars->items, round, abort_flag, status, kFaMma);
+        if (idx < 0 || idx >= total) break;
+        const FwdItem it = fwd_decode(idx, npairs, H, B);
+        const int nA = 2 * it.pr + 1, nB = 2 * it.pr + 2;
+        ok = wait(&bars->q_full, round & 1, abort_flag, status, kFaMma);
+        if (ok) ok = issue_s(0, kv) && issue_s(1, kv);
+        for (int j = 0; j < nB && ok; ++j) {
+          // S of the next key tile goes ahead of this tile's P V: the softmax has already
+          // moved S_j into registers, so the tensor core computes S_{j+1} while it runs.
+          if (j < nA) {
+            if (j + 1 < nA && !(ok = issue_s(0, kv + j + 1))) break;
+            if (!(ok = issue_pv(0, kv + j, j == 0))) break;
+          }
+          if (j + 1 < nB) {
+            if (!(ok = issue_s(1, kv + j + 1))) break;
+            if (j + 1 == nB - 1) umma_commit(&bars->q_empty);  // last S of this item issued
+          }
+          if (!(ok = issue_pv(1, kv + j, j == 0))) break;
+          umma_commit(&bars->kv_empty[(kv + j) % KV_STAGES]);
         }
-        if (j + 1 < nkv[1] && !issue_s(1, j + 1)) break;
-        if (!issue_pv(1, j)) break;
-        umma_commit(&bars->kv_empty[j % KV_STAGES]);
+        kv += nB;
       }
     }
   } else {
@@ -194,108 +303,108 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The output accumulates in TMEM; it is rescaled there only when a row's running
     // max grows by more than 2^8, otherwise P is formed against the stale max (P <= 256).
     const int w = (warp - 2) >> 2;
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;
-    const int qt = 2 * pr + w;  // query tile index
-    const int q = qt * BQ + r;  // position in the sequence
-    const int n = nkv[w];
     const uint32_t lane_base = tmem + w * 256 + (static_cast<uint32_t>(quarter * 32) << 16);
     constexpr float kRescaleThreshold = 8.0f;  // log2 units
-    float m = -INFINITY, l = 0.f;
+    uint32_t g = 0;                            // S tiles consumed by this slot
     bool ok = true;
-    for (int j = 0; j < n && ok; ++j) {
-      if (!warp_wait(&bars->s_full[w], j & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sr[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) tmem_ld32(lane_base + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->s_free[w]);  // S is in registers; the next S may overwrite it
-      const bool diag = (j == n - 1);
-      const int lim = diag ? q - j * BKV : BKV;  // columns <= lim are visible
-      // row max with 8 independent partial maxima (short dependency chains)
-      float mp[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
-      if (!diag) {
-#pragma unroll
-        for (int i = 0; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[i]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], i <= lim ? __uint_as_float(sr[i]) : -INFINITY);
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-      const float m_cand = mx * scale_log2;
-      float alpha = 1.f;
-      bool rescale = false;
-      if (j == 0) {
-        m = m_cand;
-      } else if (m_cand > m + kRescaleThreshold) {
-        alpha = ex2(m - m_cand);
-        m = m_cand;
-        rescale = true;
-      }
-      // P V of the previous tile must be done before P is overwritten or O is rescaled.
-      if (j > 0 && !warp_wait(&bars->p_empty[w], (j - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
-      // P = exp2(s*scale - m) into the swizzled K-major layout (row r, 16 chunks of 8 keys);
-      // 8 partial row sums.
-      float sp[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) sp[u] = 0.f;
-      const float neg_m = -m;
-      uint8_t* prow = sP + w * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint32_t wv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i0 = c * 8 + 2 * e;
-          float p0 = ex2(fmaf(__uint_as_float(sr[i0]), scale_log2, neg_m));
-          float p1 = ex2(fmaf(__uint_as_float(sr[i0 + 1]), scale_log2, neg_m));
-          if (diag) {
-            if (i0 > lim) p0 = 0.f;
-            if (i0 + 1 > lim) p1 = 0.f;
-          }
-          sp[(2 * e) & 7] += p0;
-          sp[(2 * e + 1) & 7] += p1;
-          __half2 hp = __floats2half2_rn(p0, p1);
-          wv[e] = *reinterpret_cast<uint32_t*>(&hp);
-        }
-        const int half = c >> 3, ch = c & 7;
-        *reinterpret_cast<uint4*>(prow + half * 16384 + ((ch ^ (r & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-      }
-      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-      // Rare: bring the TMEM output to the new max (after P, when the S registers are free).
-      if (__any_sync(0xffffffffu, rescale)) {
+    for (uint32_t round = 0; ok; ++round) {
+      const int idx = ring_take_warp(&bars->items, round, abort_flag, status, kFaSoftmax);
+      if (idx < 0 || idx >= total) break;
+      const FwdItem it = fwd_decode(idx, npairs, H, B);
+      const int qt = 2 * it.pr + w;  // query tile index
+      const int q = qt * BQ + r;     // position in the sequence
+      const int n = qt + 1;          // key tiles 0 .. qt
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j, ++g) {
+        if (!warp_wait(&bars->s_full[w], g & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
         tc_fence_after();
+        uint32_t sr[BKV];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t orr[32];
-          tmem_ld32(lane_base + 128 + half * 32, orr);
-          tmem_ld_wait();
+        for (int c = 0; c < BKV / 32; ++c) tmem_ld32(lane_base + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->s_free[w]);  // S is in registers; the next S may overwrite it
+        const bool diag = (j == n - 1);
+        const int lim = diag ? q - j * BKV : BKV;  // columns <= lim are visible
+        float mp[8];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
-          tmem_st32(lane_base + 128 + half * 32, orr);
+        for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
+        if (!diag) {
+#pragma unroll
+          for (int i = 0; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], i <= lim ? __uint_as_float(sr[i]) : -INFINITY);
         }
+        const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+        const float m_cand = mx * scale_log2;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (j == 0) {
+          m = m_cand;
+        } else if (m_cand > m + kRescaleThreshold) {
+          alpha = ex2(m - m_cand);
+          m = m_cand;
+          rescale = true;
+        }
+        // P V of the previous tile must be done before P is overwritten or O is rescaled
+        // (for j = 0 the previous item's epilogue waited for it).
+        if (j > 0 && !warp_wait(&bars->p_empty[w], (g - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+        // P = exp2(s*scale - m) as fp16 pairs into TMEM (64 columns); 8 partial row sums.
+        float sp[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sp[u] = 0.f;
+        const float neg_m = -m;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t pw[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int i0 = hf * 64 + 2 * e;
+            float p0 = ex2(fmaf(__uint_as_float(sr[i0]), scale_log2, neg_m));
+            float p1 = ex2(fmaf(__uint_as_float(sr[i0 + 1]), scale_log2, neg_m));
+            if (diag) {
+              if (i0 > lim) p0 = 0.f;
+              if (i0 + 1 > lim) p1 = 0.f;
+            }
+            sp[(2 * e) & 7] += p0;
+            sp[(2 * e + 1) & 7] += p1;
+            __half2 hp = __floats2half2_rn(p0, p1);
+            pw[e] = *reinterpret_cast<uint32_t*>(&hp);
+          }
+          tmem_st32(lane_base + 128 + hf * 32, pw);
+        }
+        const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+        // Rare: bring the TMEM output to the new max.
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t orr[32];
+            tmem_ld32(lane_base + 192 + hf * 32, orr);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+            tmem_st32(lane_base + 192 + hf * 32, orr);
+          }
+        }
+        l = l * alpha + sum;
         tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[w]);
       }
-      l = l * alpha + sum;
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[w]);
-    }
-    if (ok && !warp_wait(&bars->p_empty[w], (n - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
-    if (ok) {
+      if (ok && !warp_wait(&bars->p_empty[w], (g - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
+      if (!ok) break;
       tc_fence_after();
       const float inv = 1.f / l;
-      __half* dst = out + (int64_t)(row_base + q) * d + h * D;
+      __half* dst = out + (int64_t)(it.b * T + q) * d + it.h * D;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int hf = 0; hf < 2; ++hf) {
         uint32_t orr[32];
-        tmem_ld32(lane_base + 128 + half * 32, orr);
+        tmem_ld32(lane_base + 192 + hf * 32, orr);
         tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -306,10 +415,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            __uint_as_float(orr[c * 8 + 2 * e + 1]) * inv);
             wv[e] = *reinterpret_cast<uint32_t*>(&hv);
           }
-          *reinterpret_cast<uint4*>(dst + half * 32 + c * 8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          *reinterpret_cast<uint4*>(dst + hf * 32 + c * 8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
       }
-      lse[((int64_t)b * H + h) * T + q] = (m + __log2f(l)) * 0.69314718055994530942f;
+      lse[((int64_t)it.b * H + it.h) * T + q] = (m + __log2f(l)) * 0.69314718055994530942f;
+      // The O reads above complete before the next item's first P V overwrites O: that
+      // product waits for this warp's next p_full arrival, issued after tcgen05.wait::ld.
+      tc_fence_before();
     }
   }
   tc_fence_before();
@@ -680,12 +792,18 @@ __global__ void attn_dq_finish_kernel(const float* __restrict__ dq_acc, __half* 
 using namespace jx;
 using namespace jx::fa;
 
-extern "C" int jx_attn_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int Dh, float scale,
-                           jx_stream_t stream) {
-  JX_CHECK_ARG(qkv && out && lse, "jx_attn_fwd: NULL argument");
+extern "C" int64_t jx_attn_fwd_workspace_bytes(int B, int T, int H, int Dh) {
+  (void)B, (void)T, (void)H, (void)Dh;
+  return 256;  // the work counter of the persistent kernel
+}
+
+extern "C" int jx_attn_fwd(const void* qkv, void* out, float* lse, void* workspace, int B, int T, int H, int Dh,
+                           float scale, jx_stream_t stream) {
+  JX_CHECK_ARG(qkv && out && lse && workspace, "jx_attn_fwd: NULL argument");
   JX_CHECK_ARG(Dh == 64, "jx_attn_fwd: head_dim must be 64 (got %d)", Dh);
   JX_CHECK_ARG(B > 0 && H > 0 && T > 0 && T % 256 == 0, "jx_attn_fwd: T must be a positive multiple of 256 (got %d)", T);
-  JX_CHECK_ARG(aligned16(qkv) && aligned16(out), "jx_attn_fwd: buffers must be 16-byte aligned");
+  JX_CHECK_ARG(aligned16(qkv) && aligned16(out) && aligned16(workspace), "jx_attn_fwd: buffers must be 16-byte aligned");
+  JX_CHECK_ARG((int64_t)(T / 256) * H * B < (1LL << 30), "jx_attn_fwd: too many work items");
   const int64_t rows = (int64_t)B * T;
   const int64_t cols = 3LL * H * D;
   CUtensorMap tm;
@@ -696,10 +814,14 @@ extern "C" int jx_attn_fwd(const void* qkv, void* out, float* lse, int B, int T,
                 "jx_attn_fwd: smem attribute");
     attr_set = true;
   }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int* counter = static_cast<int*>(workspace);
+  JX_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int), s), "jx_attn_fwd: clear work counter");
   const float scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid(T / (2 * BQ), H, B);
-  attn_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
-      tm, static_cast<__half*>(out), lse, T, H, scale_log2, status_ptr());
+  const int64_t items = (int64_t)(T / (2 * BQ)) * H * B;
+  const int grid = (int)std::min<int64_t>(items, num_sms());
+  attn_fwd_tc_kernel<<<grid, kFwdThreads, kSmemBytes, s>>>(tm, static_cast<__half*>(out), lse, counter, B, T, H,
+                                                           scale_log2, status_ptr());
   JX_CHECK_LAUNCH("jx_attn_fwd");
   return JX_OK;
 }

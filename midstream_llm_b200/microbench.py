@@ -197,9 +197,11 @@ def bench_attn(iters: int) -> None:
         o, lse = ops.attn_fwd(qkv, B, T, H, D)
         do = torch.randn_like(o)
         ws = torch.empty(ops.attn_bwd_workspace_bytes(B, T, H, D) // 4 + 4, device="cuda")
+        wsf = torch.empty(ops.attn_fwd_workspace_bytes(B, T, H, D) // 4 + 4, device="cuda")
         dqkv = torch.empty_like(qkv)
         fl = 2.0 * B * H * T * T * D  # causal forward: two T x T x D products, half of them
-        _emit(f"attn_fwd causal B{B} T{T} H16 D64", _time(lambda: ops.attn_fwd(qkv, B, T, H, D, out=o, lse=lse), iters),
+        _emit(f"attn_fwd causal B{B} T{T} H16 D64", _time(lambda: ops.attn_fwd(qkv, B, T, H, D, out=o, lse=lse,
+                                                                             workspace=wsf), iters),
               fl, "TFLOP/s", pk.get("bf16_tflops", 1590.0))
         _emit(f"attn_bwd causal B{B} T{T} H16 D64", _time(lambda: ops.attn_bwd(qkv, o, do, lse, B, T, H, D, out=dqkv,
                                                                               workspace=ws), iters),

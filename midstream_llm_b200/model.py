@@ -243,6 +243,7 @@ class Workspace:
     dqkv: torch.Tensor
     dgu: torch.Tensor
     attn_ws: torch.Tensor
+    attn_fwd_ws: torch.Tensor
     norm_part: torch.Tensor
     wgrad_ws: torch.Tensor
     cos: torch.Tensor
@@ -331,6 +332,7 @@ class JishuiForCausalLM(nn.Module):
             dh=torch.empty(M, d, **f16) if train else None, do=torch.empty(M, d, **f16) if train else None,
             dqkv=torch.empty(M, 3 * d, **f16) if train else None, dgu=torch.empty(M, 2 * F, **f16) if train else None,
             attn_ws=torch.empty(ops.attn_bwd_workspace_bytes(B, T, H, c.head_dim) // 4 + 4, **f32) if train else None,
+            attn_fwd_ws=torch.empty(ops.attn_fwd_workspace_bytes(B, T, H, c.head_dim) // 4 + 4, **f32),
             norm_part=torch.empty(nparts * d, **f32), wgrad_ws=torch.empty(max(wmax // 4, 4), **f32),
             cos=cos, sin=sin)
         self._ws[key] = ws
@@ -364,7 +366,7 @@ class JishuiForCausalLM(nn.Module):
         d, F, H, hd = c.hidden_size, c.intermediate_size, c.num_attention_heads, c.head_dim
         ops.rmsnorm_fwd(x_in, w["g1"], c.norm_eps, out=A.h1, rstd=A.rstd1)
         ops.gemm_qkv_rope(A.h1, w["wqkv"], d, ws.cos, ws.sin, T, hd, out=A.qkv)
-        ops.attn_fwd(A.qkv, B, T, H, hd, out=A.o, lse=A.lse)
+        ops.attn_fwd(A.qkv, B, T, H, hd, out=A.o, lse=A.lse, workspace=ws.attn_fwd_ws)
         ops.gemm_f16(A.o, w["wo"], resid=x_in, out=A.xmid)
         ops.rmsnorm_fwd(A.xmid, w["g2"], c.norm_eps, out=A.h2, rstd=A.rstd2)
         ops.gemm_swiglu_fwd(A.h2, w["wgu"], F, gate=A.gate, up=A.up, act=A.act)

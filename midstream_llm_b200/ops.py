@@ -218,12 +218,22 @@ def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, g: torch.Tensor, accumulate: b
 
 
 # ---------------------------------------------------------------- attention
+def attn_fwd_workspace_bytes(B: int, T: int, H: int, D: int) -> int:
+    return _lib.query("jx_attn_fwd_workspace_bytes", B, T, H, D)
+
+
 def attn_fwd(qkv: torch.Tensor, B: int, T: int, H: int, D: int, out: torch.Tensor | None = None,
-             lse: torch.Tensor | None = None):
+             lse: torch.Tensor | None = None, workspace: torch.Tensor | None = None):
+    """Causal attention forward: (out f16 [B*T, H*D], lse f32 [B, H, T]). `workspace` holds the
+    kernel's work counter; without one a fresh buffer is taken from torch's allocator."""
     _check(qkv, F16, "qkv")
     o = out if out is not None else torch.empty(B * T, H * D, device=qkv.device, dtype=F16)
     lse = lse if lse is not None else torch.empty(B, H, T, device=qkv.device, dtype=F32)
-    _lib.call("jx_attn_fwd", qkv.data_ptr(), o.data_ptr(), lse.data_ptr(), B, T, H, D, 1.0 / math.sqrt(D), _stream())
+    need = attn_fwd_workspace_bytes(B, T, H, D)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need // 4 + 4, device=qkv.device, dtype=F32)
+    _lib.call("jx_attn_fwd", qkv.data_ptr(), o.data_ptr(), lse.data_ptr(), workspace.data_ptr(), B, T, H, D,
+              1.0 / math.sqrt(D), _stream())
     return o, lse
 
 

@@ -38,7 +38,7 @@ def test_pure_host_queries():
 def test_invalid_arguments_are_rejected_with_text():
     from midstream_llm_b200 import _lib
     with pytest.raises(_lib.JxError, match="head_dim must be 64"):
-        _lib.call("jx_attn_fwd", 16, 16, 16, 1, 128, 1, 32, 0.125, None)
+        _lib.call("jx_attn_fwd", 16, 16, 16, 16, 1, 128, 1, 32, 0.125, None)
     with pytest.raises(_lib.JxError, match="cols must be a multiple of 8"):
         _lib.call("jx_rmsnorm_fwd", 16, None, None, 16, 16, 16, 4, 12, 1e-5, None)
 
