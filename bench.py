@@ -278,7 +278,8 @@ def main() -> None:
     line = None
     if rank == 0:
         gemm_flops = sum(p[0] for p in prof)
-        gemm_ms = sum(p[1].elapsed_time(p[2]) for p in prof)
+        gemm_ms = sum(p[2].elapsed_time(p[3]) for p in prof)
+        gemm_bytes = sum(p[1] for p in prof) / max(len(prof), 1)
         gemm_tflops = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
         peak = pk["bf16_tflops_sustained"] if "bf16_tflops_sustained" in pk else pk["bf16_tflops"]
         traffic = None
@@ -302,6 +303,7 @@ def main() -> None:
                          "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": (gemm_tflops / peak) if gemm_tflops else None, "traffic": traffic,
                          "launches": len(prof), "share_of_step": gemm_ms / ms if ms > 0 else None,
+                         "algorithmic_bytes_per_launch": gemm_bytes,
                          "peak_note": f"bf16_tflops_sustained ({pk_kind})"},
             "gpu_launches": launches,
             "clocks": clock_info,

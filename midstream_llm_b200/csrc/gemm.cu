@@ -116,6 +116,19 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& mb, int
 
 __device__ __forceinline__ float h2f_round(float x) { return __half2float(__float2half_rn(x)); }
 
+// Round a and b to fp16 and back (round to nearest even), two values per packed conversion.
+__device__ __forceinline__ void round2(float& a, float& b) {
+  const float2 f = __half22float2(__floats2half2_rn(a, b));
+  a = f.x;
+  b = f.y;
+}
+
+template <int N>
+__device__ __forceinline__ void round_all(float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; i += 2) round2(v[i], v[i + 1]);
+}
+
 // Raw 16-byte loads of 32 consecutive fp16 values of one row (zero outside [M, N)).
 __device__ __forceinline__ void load_raw32(const __half* base, int64_t ld, int row, int col, int M, int N,
                                            uint4 (&r)[4]) {
@@ -257,10 +270,12 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
           float a[32], b[32];
           unpack32(q0, a);
           unpack32(q1, b);
+          round_all(v0);
+          round_all(v1);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            v0[i] = a[i] + h2f_round(v0[i]);
-            v1[i] = b[i] + h2f_round(v1[i]);
+            v0[i] = a[i] + v0[i];
+            v1[i] = b[i] + v1[i];
           }
         }
         st.begin();
@@ -281,11 +296,14 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
                 *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
           } else {
             float* dst = p.G + (int64_t)row * p.ldg + col;
+            float vr[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) vr[i] = v[i];
+            round_all(vr);
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
               if (col + g * 4 + 4 <= p.N) {
-                float4 o = make_float4(h2f_round(v[g * 4]), h2f_round(v[g * 4 + 1]), h2f_round(v[g * 4 + 2]),
-                                       h2f_round(v[g * 4 + 3]));
+                float4 o = make_float4(vr[g * 4], vr[g * 4 + 1], vr[g * 4 + 2], vr[g * 4 + 3]);
                 if (p.accumulate) {
                   const float4 old = *reinterpret_cast<const float4*>(dst + g * 4);
                   o.x += old.x;
@@ -324,8 +342,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int i = i4 * 4 + j;
-            const float x0 = h2f_round(a[i]);
-            const float x1 = h2f_round(b[i]);
+            float x0 = a[i], x1 = b[i];
+            round2(x0, x1);
             a[i] = __fsub_rn(__fmul_rn(x0, cc[j]), __fmul_rn(x1, ss[j]));
             b[i] = __fadd_rn(__fmul_rn(x0, ss[j]), __fmul_rn(x1, cc[j]));
           }
@@ -349,11 +367,15 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
       float g0[32], g1[32], u0[32], u1[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        g0[i] = h2f_round(__uint_as_float(rg0[i]));
-        g1[i] = h2f_round(__uint_as_float(rg1[i]));
-        u0[i] = h2f_round(__uint_as_float(ru0[i]));
-        u1[i] = h2f_round(__uint_as_float(ru1[i]));
+        g0[i] = __uint_as_float(rg0[i]);
+        g1[i] = __uint_as_float(rg1[i]);
+        u0[i] = __uint_as_float(ru0[i]);
+        u1[i] = __uint_as_float(ru1[i]);
       }
+      round_all(g0);
+      round_all(g1);
+      round_all(u0);
+      round_all(u1);
       st.begin();
       st.put32(0, g0);
       st.put32(1, g1);
@@ -364,8 +386,15 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
       st.flush(om.c1, col, yrow);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        g0[i] = __fmul_rn(h2f_round(silu_f(g0[i])), u0[i]);
-        g1[i] = __fmul_rn(h2f_round(silu_f(g1[i])), u1[i]);
+        g0[i] = silu_f(g0[i]);
+        g1[i] = silu_f(g1[i]);
+      }
+      round_all(g0);
+      round_all(g1);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        g0[i] = __fmul_rn(g0[i], u0[i]);
+        g1[i] = __fmul_rn(g1[i], u1[i]);
       }
       st.begin();
       st.put32(0, g0);
@@ -395,14 +424,20 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
         to_f32(part ? r1 : r0, d);
         unpack32(part ? g1 : g0, g);
         unpack32(part ? u1 : u0, u);
+        float sig[32], s16[32], ds[32];
+        round_all(d);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float d16 = h2f_round(d[i]);
-          const float sig = sigmoid_f(g[i]);
-          const float s16 = h2f_round(g[i] * sig);
-          du[part][i] = __fmul_rn(d16, s16);
-          const float ds = h2f_round(__fmul_rn(d16, u[i]));
-          dg[part][i] = __fmul_rn(__fmul_rn(ds, sig), 1.0f + __fmul_rn(g[i], 1.0f - sig));
+          sig[i] = sigmoid_f(g[i]);
+          s16[i] = g[i] * sig[i];
+          ds[i] = __fmul_rn(d[i], u[i]);
+        }
+        round_all(s16);
+        round_all(ds);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          du[part][i] = __fmul_rn(d[i], s16[i]);
+          dg[part][i] = __fmul_rn(__fmul_rn(ds[i], sig[i]), 1.0f + __fmul_rn(g[i], 1.0f - sig[i]));
         }
       }
       st.begin();

@@ -26,10 +26,13 @@ def set_gemm_profile(records: list | None) -> None:
 
 
 class _GemmTimer:
-    __slots__ = ("flops", "start")
+    """Records (flops, algorithmic bytes, start event, end event) of one GEMM launch when profiling is on.
+    Algorithmic bytes: each operand read once and each output written once (fp16 2 B, fp32 4 B)."""
+    __slots__ = ("flops", "bytes", "start")
 
-    def __init__(self, flops: float):
+    def __init__(self, flops: float, nbytes: float = 0.0):
         self.flops = flops
+        self.bytes = nbytes
         self.start = None
 
     def __enter__(self):
@@ -42,7 +45,7 @@ class _GemmTimer:
         if self.start is not None and _GEMM_PROFILE is not None:
             end = torch.cuda.Event(enable_timing=True)
             end.record()
-            _GEMM_PROFILE.append((self.flops, self.start, end))
+            _GEMM_PROFILE.append((self.flops, self.bytes, self.start, end))
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -148,7 +151,7 @@ def gemm_f16(a: torch.Tensor, b: torch.Tensor, a_mn_major: bool = False, b_mn_ma
     c = out if out is not None else torch.empty(M, N, device=a.device, dtype=F16)
     if resid is not None:
         _check(resid, F16, "resid", contiguous=False)
-    with _GemmTimer(2.0 * M * N * K):
+    with _GemmTimer(2.0 * M * N * K, 2.0 * (M * K + N * K + M * N * (2 if resid is not None else 1))):
         _lib.call("jx_gemm_f16", a.data_ptr(), _ld(a), int(a_mn_major), b.data_ptr(), _ld(b), int(b_mn_major), M, N,
                   K, c.data_ptr(), _ld(c), _ptr(resid), _ld(resid) if resid is not None else 0, _stream())
     return c
@@ -162,7 +165,7 @@ def gemm_qkv_rope(x: torch.Tensor, w: torch.Tensor, hidden: int, cos: torch.Tens
     _check(sin, F32, "sin")
     M, K = x.shape
     c = out if out is not None else torch.empty(M, 3 * hidden, device=x.device, dtype=F16)
-    with _GemmTimer(2.0 * M * 3 * hidden * K):
+    with _GemmTimer(2.0 * M * 3 * hidden * K, 2.0 * (M * K + 3 * hidden * K + M * 3 * hidden)):
         _lib.call("jx_gemm_qkv_rope", x.data_ptr(), K, w.data_ptr(), M, hidden, K, c.data_ptr(), _ld(c),
                   cos.data_ptr(), sin.data_ptr(), seq_len, head_dim, _stream())
     return c
@@ -176,7 +179,7 @@ def gemm_swiglu_fwd(x: torch.Tensor, wgu: torch.Tensor, F: int, gate=None, up=No
     gate = gate if gate is not None else mk()
     up = up if up is not None else mk()
     act = act if act is not None else mk()
-    with _GemmTimer(2.0 * M * 2 * F * K):
+    with _GemmTimer(2.0 * M * 2 * F * K, 2.0 * (M * K + 2 * F * K + 3 * M * F)):
         _lib.call("jx_gemm_swiglu_fwd", x.data_ptr(), K, wgu.data_ptr(), M, F, K, gate.data_ptr(), up.data_ptr(),
                   act.data_ptr(), F, _stream())
     return gate, up, act
@@ -190,7 +193,7 @@ def gemm_swiglu_bwd(dy: torch.Tensor, wd: torch.Tensor, gate: torch.Tensor, up: 
     M, K = dy.shape
     F = wd.shape[1]
     dgu = out if out is not None else torch.empty(M, 2 * F, device=dy.device, dtype=F16)
-    with _GemmTimer(2.0 * M * F * K):
+    with _GemmTimer(2.0 * M * F * K, 2.0 * (M * K + F * K + 2 * M * F + 2 * M * F)):
         _lib.call("jx_gemm_swiglu_bwd", dy.data_ptr(), K, wd.data_ptr(), M, F, K, gate.data_ptr(), up.data_ptr(), F,
                   dgu.data_ptr(), _ld(dgu), _stream())
     return dgu
@@ -212,7 +215,7 @@ def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, g: torch.Tensor, accumulate: b
         need = wgrad_workspace_bytes(N, K, splits)
         if workspace is None or workspace.numel() * workspace.element_size() < need:
             workspace = torch.empty(need // 4 + 1, device=dy.device, dtype=F32)
-    with _GemmTimer(2.0 * T * N * K):
+    with _GemmTimer(2.0 * T * N * K, 2.0 * (T * N + T * K) + 4.0 * N * K * (2 if accumulate else 1)):
         _lib.call("jx_gemm_wgrad", dy.data_ptr(), _ld(dy), x.data_ptr(), _ld(x), T, N, K, g.data_ptr(), _ld(g),
                   int(accumulate), splits, _ptr(workspace), _stream())
 
