@@ -435,34 +435,43 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 // ---------------------------------------------------------------------------
 // Backward on tcgen05. One CTA per (128-key block, head, batch); the key
 // block's K and V stay in shared memory, dK and dV accumulate in TMEM across
-// the query tiles i = kb .. T/128-1. Per query tile (Q_i, dO_i, LSE_i, Delta_i
-// double-buffered by TMA):
-//   S^T  = K Q_i^T     (M 128 keys, N 128 queries, K 64)   TMEM [0,128)
-//   dP^T = V dO_i^T    (M 128, N 128, K 64)                TMEM [128,256)
-//   softmax warps: P^T = exp(S^T*scale - LSE), dS^T = P^T (dP^T - Delta),
-//                  both fp16 into 128B-swizzled shared memory
-//   dV += P^T dO_i     (M 128, N 64, K 128; dO read MN-major)  TMEM [256,320)
-//   dK += dS^T Q_i     (M 128, N 64, K 128; Q read MN-major)   TMEM [320,384)
-//   dQ_i = dS K        (M 128 queries, N 64, K 128 keys; dS^T read MN-major
-//                       as the A operand, K read MN-major)     TMEM [384,512), two buffers
-//   dQ_i is added to an fp32 accumulator in global memory (vector reductions)
-//   while the MMAs of tile i+1 run.
+// the query tiles i = kb .. T/128-1. Each query tile (Q_i, dO_i, LSE_i,
+// Delta_i double-buffered by TMA) is processed as two halves of 64 queries,
+// pipelined against each other:
+//   S^T_h  = K Q_h^T   (M 128 keys, N 64 queries, K 64)    TMEM [64h, 64h+64)
+//   dP^T_h = V dO_h^T  (M 128, N 64, K 64)                 TMEM [128+64h, ...)
+//   softmax warps of half h: P^T = exp(S^T*scale - LSE), dS^T = P^T (dP^T - Delta);
+//                  both written back to TMEM as fp16 pairs over the columns just
+//                  read, and dS^T also to 128B-swizzled shared memory (two buffers)
+//   dV += P^T_h dO_h   (M 128, N 64, K 64; P^T from TMEM, dO read MN-major)   TMEM [256,320)
+//   dK += dS^T_h Q_h   (M 128, N 64, K 64; dS^T from TMEM, Q read MN-major)   TMEM [320,384)
+//   then S^T_h / dP^T_h of tile i+1 (the tensor core runs one thread's products
+//   in issue order, so they follow the dV / dK reads of those columns); while
+//   the softmax of one half runs, the tensor core works on the other half.
+//   dQ_i = dS K        (M 128 queries, N 64, K 128 keys; dS^T in shared memory
+//                       read MN-major as the A operand, K read MN-major)     TMEM [384,512), two buffers
+//   dQ_i is added to an fp32 accumulator in global memory by TMA reduce-add
+//   while the products of tile i+1 run.
 // Warps: 0 TMA producer, 1 MMA issuer, 2..9 softmax / epilogue (two warps per
-// TMEM lane quarter, each on half of the columns).
+// TMEM lane quarter, each on half of the query columns).
 // ---------------------------------------------------------------------------
 constexpr int kBwdThreads = 320;
 constexpr uint32_t kDqStageBytes = 32 * 32 * 4;  // one warp's [32 rows x 32 cols] fp32 dQ block
-constexpr size_t kBwdSmem = 1024 + 2 * kTileBytes /*K,V*/ + 4 * kTileBytes /*Q,dO x2*/ + 2 * kPBytes /*P^T, dS^T*/ +
+constexpr size_t kBwdSmem = 1024 + 2 * kTileBytes /*K,V*/ + 4 * kTileBytes /*Q,dO x2*/ + 2 * kPBytes /*dS^T x2*/ +
                             8 * kDqStageBytes /*dQ staging*/ + 2 * 2 * BQ * sizeof(float) /*LSE, Delta x2*/ + 512;
 
 struct BwdBars {
   uint64_t kv_full;
   uint64_t q_full[2], q_empty[2];
-  uint64_t sdp_full, sdp_free;
-  uint64_t p_full, grads_done, dq_free[2];
+  uint64_t sdp_full[2], p_full[2], grads_done, dq_free[2];  // sdp / p per query half
   uint32_t tmem_base;
   int abort;
 };
+
+// TMEM column (relative to the S^T or dP^T base) of the fp16 pair holding queries
+// 2c, 2c+1 of K step kk (16 queries): the softmax warp of column half h writes the
+// pairs of queries [64h, 64h+64) as two 16-column chunks at 64h and 64h+16.
+__device__ __forceinline__ uint32_t pair_col(int kk) { return (kk >> 2) * 64 + (kk & 3) * 8; }
 
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -494,9 +503,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = sK + kTileBytes;
   uint8_t* sQ = sV + kTileBytes;             // 2 stages
   uint8_t* sO = sQ + 2 * kTileBytes;         // dO, 2 stages
-  uint8_t* sPt = sO + 2 * kTileBytes;        // P^T  [128 keys x 128 queries]
-  uint8_t* sSt = sPt + kPBytes;              // dS^T [128 keys x 128 queries]
-  uint8_t* sDq = sSt + kPBytes;              // [8 warps][32 x 32] fp32 dQ staging (128B-swizzled)
+  uint8_t* sSt = sO + 2 * kTileBytes;        // dS^T [128 keys x 128 queries], 2 buffers (tile parity)
+  uint8_t* sDq = sSt + 2 * kPBytes;          // [8 warps][32 x 32] fp32 dQ staging (128B-swizzled)
   float* sL = reinterpret_cast<float*>(sDq + 8 * kDqStageBytes);  // [2][128]
   float* sD = sL + 2 * BQ;                               // [2][128]
   BwdBars* bars = reinterpret_cast<BwdBars*>(sD + 2 * BQ);
@@ -510,6 +518,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int row_base = b * T;
   const int ntiles = nqb - kb;  // query tiles kb .. nqb-1
   const float log2e = 1.4426950408889634f;
+  (void)dq_acc;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->kv_full, 1);
@@ -517,9 +526,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&bars->q_full[s], 1);
       mbar_init(&bars->q_empty[s], 1);
     }
-    mbar_init(&bars->sdp_full, 1);
-    mbar_init(&bars->sdp_free, 8);
-    mbar_init(&bars->p_full, 8);
+    for (int hf = 0; hf < 2; ++hf) {
+      mbar_init(&bars->sdp_full[hf], 1);
+      mbar_init(&bars->p_full[hf], 4);
+    }
     mbar_init(&bars->grads_done, 1);
     mbar_init(&bars->dq_free[0], 8);
     mbar_init(&bars->dq_free[1], 8);
@@ -557,60 +567,71 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t id_sq = idesc_f16_f32(BKV, BQ, false, false);
+      constexpr uint32_t id_sq = idesc_f16_f32(BKV, BQ / 2, false, false);
       constexpr uint32_t id_kn = idesc_f16_f32(BKV, D, false, true);
       constexpr uint32_t id_q = idesc_f16_f32(BQ, D, true, true);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      const uint32_t pt_addr = smem_u32(sPt), st_addr = smem_u32(sSt);
-      bool ok = wait(&bars->kv_full, 0, abort_flag, status, kFaMma);
-      // S^T = K Q_t^T and dP^T = V dO_t^T into TMEM [0,256) once the softmax has moved the
-      // previous tile's scores into registers.
-      auto issue_sdp = [&](int t) -> bool {
-        const int s = t & 1;
-        if (!wait(&bars->q_full[s], (t >> 1) & 1, abort_flag, status, kFaMma)) return false;
-        if (!wait(&bars->sdp_free, (t & 1) ^ 1, abort_flag, status, kFaMma)) return false;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), o_addr = smem_u32(sO + s * kTileBytes);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), st_addr = smem_u32(sSt);
+      // S^T / dP^T of query half hf of tile t: M 128 keys, N 64 queries, into TMEM columns
+      // [64 hf, 64 hf + 64) and [128 + 64 hf, ...).
+      auto issue_sdp = [&](int t, int hf) {
+        const uint32_t q_addr = smem_u32(sQ + (t & 1) * kTileBytes) + hf * 8192;
+        const uint32_t o_addr = smem_u32(sO + (t & 1) * kTileBytes) + hf * 8192;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          umma_f16(tmem, smem_desc_sw128(k_addr + kk * 32, 16, 1024), smem_desc_sw128(q_addr + kk * 32, 16, 1024),
-                   id_sq, kk > 0 ? 1u : 0u);
-          umma_f16(tmem + 128, smem_desc_sw128(v_addr + kk * 32, 16, 1024),
+          umma_f16(tmem + hf * 64, smem_desc_sw128(k_addr + kk * 32, 16, 1024),
+                   smem_desc_sw128(q_addr + kk * 32, 16, 1024), id_sq, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 128 + hf * 64, smem_desc_sw128(v_addr + kk * 32, 16, 1024),
                    smem_desc_sw128(o_addr + kk * 32, 16, 1024), id_sq, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars->sdp_full);
-        return true;
+        umma_commit(&bars->sdp_full[hf]);
       };
-      if (ok) ok = issue_sdp(0);
+      bool ok = wait(&bars->kv_full, 0, abort_flag, status, kFaMma) &&
+                wait(&bars->q_full[0], 0, abort_flag, status, kFaMma);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0, 0);
+        issue_sdp(0, 1);
+      }
       for (int t = 0; t < ntiles && ok; ++t) {
         const int s = t & 1;
-        // The next tile's scores are computed while the softmax of this tile runs.
-        if (t + 1 < ntiles && !issue_sdp(t + 1)) break;
         const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), o_addr = smem_u32(sO + s * kTileBytes);
-        if (!wait(&bars->p_full, t & 1, abort_flag, status, kFaMma)) break;
-        if (!wait(&bars->dq_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, status, kFaMma)) break;
-        tc_fence_after();
+        for (int hf = 0; hf < 2 && ok; ++hf) {
+          // P^T / dS^T of this half are in TMEM (over its S^T / dP^T columns).
+          if (!(ok = wait(&bars->p_full[hf], t & 1, abort_flag, status, kFaMma))) break;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;  // K-major step over queries
-          umma_f16(tmem + 256, smem_desc_sw128(pt_addr + koff, 16, 1024), smem_desc_sw128(o_addr + kk * 2048, 8192, 1024),
-                   id_kn, (t > 0 || kk > 0) ? 1u : 0u);
-          umma_f16(tmem + 320, smem_desc_sw128(st_addr + koff, 16, 1024), smem_desc_sw128(q_addr + kk * 2048, 8192, 1024),
-                   id_kn, (t > 0 || kk > 0) ? 1u : 0u);
+          for (int j = 0; j < 4; ++j) {
+            const int kk = hf * 4 + j;  // 16 queries per step
+            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+            umma_f16_ts(tmem + 256, tmem + pair_col(kk), smem_desc_sw128(o_addr + kk * 2048, 8192, 1024), id_kn, acc);
+            umma_f16_ts(tmem + 320, tmem + 128 + pair_col(kk), smem_desc_sw128(q_addr + kk * 2048, 8192, 1024), id_kn,
+                        acc);
+          }
+          if (hf == 1) umma_commit(&bars->q_empty[s]);  // Q_t / dO_t are no longer read
+          // The next tile's scores of this half overwrite the columns dV / dK just read; the
+          // tensor core runs a thread's products in issue order.
+          if (t + 1 < ntiles) {
+            if (hf == 0 && !(ok = wait(&bars->q_full[(t + 1) & 1], ((t + 1) >> 1) & 1, abort_flag, status, kFaMma)))
+              break;
+            issue_sdp(t + 1, hf);
+          }
         }
+        if (!ok) break;
+        if (!(ok = wait(&bars->dq_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, status, kFaMma))) break;
+        tc_fence_after();
+        const uint32_t sbuf = st_addr + s * kPBytes;
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
           // dS^T read MN-major: queries contiguous (two 64-query halves 16 KiB apart), 16 keys per step.
-          umma_f16(tmem + 384 + (t & 1) * D, smem_desc_sw128(st_addr + kk * 2048, 16384, 1024),
+          umma_f16(tmem + 384 + (t & 1) * D, smem_desc_sw128(sbuf + kk * 2048, 16384, 1024),
                    smem_desc_sw128(k_addr + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->grads_done);
-        umma_commit(&bars->q_empty[s]);
       }
     }
   } else {
     const int quarter = warp & 3;         // TMEM lane quarter
-    const int colh = (warp - 2) >> 2;     // which half of the columns
+    const int colh = (warp - 2) >> 2;     // which half of the query columns
     const int r = quarter * 32 + lane;    // key row (S^T / dP^T / dK / dV) or query row (dQ)
     const int key = kb * BKV + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -646,34 +667,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     };
     bool ok = true;
+    uint8_t* srow0 = sSt + colh * 16384 + (r >> 3) * 1024 + (r & 7) * 128;  // this thread's dS^T row
     for (int t = 0; t < ntiles && ok; ++t) {
       const int s = t & 1, qi = kb + t;
       const bool diag = (t == 0);
       if (!wait(&bars->q_full[s], (t >> 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
-      if (!warp_wait(&bars->sdp_full, t & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      if (!warp_wait(&bars->sdp_full[colh], t & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+      uint8_t* srow = srow0 + s * kPBytes;
       tc_fence_after();
       const float* Ls = sL + s * BQ;
       const float* Ds = sD + s * BQ;
-      // P^T and dS^T for this warp's 64 query columns, packed as fp16 pairs.
-      uint32_t pw[32], sw[32];
-      const int lim = diag ? key - qi * BQ : -1;  // on the diagonal tile, queries at index < lim... are masked
+      const int lim = diag ? key - qi * BQ : -1;  // on the diagonal tile, queries at index < lim are masked
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch) {
+        // 32 queries: S^T / dP^T in, P^T / dS^T (fp16 pairs) back over the first 16 columns of
+        // this warp's half (already read), dS^T also to shared memory.
+        const int q0 = colh * 64 + ch * 32;
         uint32_t sr[32], dr[32];
-        tmem_ld32(lane_base + colh * 64 + ch * 32, sr);
-        tmem_ld32(lane_base + 128 + colh * 64 + ch * 32, dr);
+        tmem_ld32(lane_base + q0, sr);
+        tmem_ld32(lane_base + 128 + q0, dr);
         tmem_ld_wait();
-        const int q0 = colh * 64 + ch * 32;  // first query index of this chunk within the tile
+        uint32_t pw[16], sw[16];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {  // 4 queries per group: LSE / Delta as float4 (broadcast reads)
-          const float4 L4 = *reinterpret_cast<const float4*>(Ls + q0 + g * 4);
-          const float4 D4 = *reinterpret_cast<const float4*>(Ds + q0 + g * 4);
+        for (int gq = 0; gq < 8; ++gq) {  // 4 queries per group: LSE / Delta as float4 (broadcast reads)
+          const float4 L4 = *reinterpret_cast<const float4*>(Ls + q0 + gq * 4);
+          const float4 D4 = *reinterpret_cast<const float4*>(Ds + q0 + gq * 4);
           const float nl[4] = {-L4.x * log2e, -L4.y * log2e, -L4.z * log2e, -L4.w * log2e};
           const float dl[4] = {D4.x, D4.y, D4.z, D4.w};
           float pv[4], dv[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const int qc = g * 4 + u;
+            const int qc = gq * 4 + u;
             float p = ex2(fmaf(__uint_as_float(sr[qc]), scale_log2, nl[u]));
             if (diag && q0 + qc < lim) p = 0.f;
             pv[u] = p;
@@ -681,30 +705,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           __half2 hp0 = __floats2half2_rn(pv[0], pv[1]), hp1 = __floats2half2_rn(pv[2], pv[3]);
           __half2 hs0 = __floats2half2_rn(dv[0], dv[1]), hs1 = __floats2half2_rn(dv[2], dv[3]);
-          pw[ch * 16 + g * 2] = *reinterpret_cast<uint32_t*>(&hp0);
-          pw[ch * 16 + g * 2 + 1] = *reinterpret_cast<uint32_t*>(&hp1);
-          sw[ch * 16 + g * 2] = *reinterpret_cast<uint32_t*>(&hs0);
-          sw[ch * 16 + g * 2 + 1] = *reinterpret_cast<uint32_t*>(&hs1);
+          pw[gq * 2] = *reinterpret_cast<uint32_t*>(&hp0);
+          pw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hp1);
+          sw[gq * 2] = *reinterpret_cast<uint32_t*>(&hs0);
+          sw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hs1);
+        }
+        tmem_st16(lane_base + colh * 64 + ch * 16, pw);
+        tmem_st16(lane_base + 128 + colh * 64 + ch * 16, sw);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // 4 chunks of 8 queries
+          const int off = ((ch * 4 + c) ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(srow + off) = make_uint4(sw[c * 4], sw[c * 4 + 1], sw[c * 4 + 2], sw[c * 4 + 3]);
         }
       }
+      tmem_st_wait();
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sdp_free);
-      // The previous tile's MMAs must be done reading P^T / dS^T before they are overwritten.
-      if (t > 0 && !warp_wait(&bars->grads_done, (t - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
-      uint8_t* prow = sPt + colh * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
-      uint8_t* srow = sSt + colh * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 queries
-        const int off = (c ^ (r & 7)) << 4;
-        *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[c * 4], pw[c * 4 + 1], pw[c * 4 + 2], pw[c * 4 + 3]);
-        *reinterpret_cast<uint4*>(srow + off) = make_uint4(sw[c * 4], sw[c * 4 + 1], sw[c * 4 + 2], sw[c * 4 + 3]);
-      }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full);
-      // The previous tile's dQ is complete (grads_done(t-1)); reduce it while this tile's MMAs run.
-      if (t > 0) drain_dq(t - 1);
+      if (lane == 0) mbar_arrive(&bars->p_full[colh]);
+      // The previous tile's dQ completed before this tile's scores; reduce it while this tile's products run.
+      if (t > 0) {
+        if (!warp_wait(&bars->grads_done, (t - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+        drain_dq(t - 1);
+      }
     }
     if (ok && !warp_wait(&bars->grads_done, (ntiles - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
     if (ok) drain_dq(ntiles - 1);
