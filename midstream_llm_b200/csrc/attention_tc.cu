@@ -241,17 +241,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
       uint32_t kv = 0;
       uint32_t ns[2] = {0, 0}, np[2] = {0, 0};  // S tiles issued / P V products issued per slot
+      // Descriptors built once, advanced by constant additions per product.
+      const uint64_t dQ0 = smem_desc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), 8192, 1024);
       auto issue_s = [&](int w, uint32_t kvi) -> bool {
         const int s = kvi % KV_STAGES;
         if (!wait(&bars->kv_full[s], (kvi / KV_STAGES) & 1, abort_flag, status, kFaMma)) return false;
         if (!wait(&bars->s_free[w], (ns[w] & 1) ^ 1, abort_flag, status, kFaMma)) return false;
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + w * kTileBytes);
-        const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
+        const uint64_t a = desc_adv(dQ0, w * kTileBytes), bk = desc_adv(dK0, s * kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16(tmem + w * 256, smem_desc_sw128(q_addr + kk * 32, 16, 1024),
-                   smem_desc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + w * 256, desc_adv(a, kk * 32), desc_adv(bk, kk * 32), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(&bars->s_full[w]);
         ++ns[w];
         return true;
@@ -260,12 +262,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int s = kvi % KV_STAGES;
         if (!wait(&bars->p_full[w], np[w] & 1, abort_flag, status, kFaMma)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + s * kTileBytes);
+        const uint64_t bv = desc_adv(dV0, s * kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
           // P from TMEM (16 keys = 8 packed columns per step); V [128 keys x 64 hd] read
           // MN-major (hd contiguous), 16 keys = two 8-row groups.
-          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
+          const uint64_t bdesc = desc_adv(bv, kk * 2048);
           umma_f16_ts(tmem + w * 256 + 192, tmem + w * 256 + 128 + kk * 8, bdesc, idesc_o,
                       (!first || kk > 0) ? 1u : 0u);
         }
@@ -570,18 +572,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t id_sq = idesc_f16_f32(BKV, BQ / 2, false, false);
       constexpr uint32_t id_kn = idesc_f16_f32(BKV, D, false, true);
       constexpr uint32_t id_q = idesc_f16_f32(BQ, D, true, true);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), st_addr = smem_u32(sSt);
+      // Shared-memory descriptors are built once and advanced by constant additions: one
+      // thread issues every product, and an N = 64 product is shorter than building two
+      // descriptors from addresses.
+      const uint64_t dK = smem_desc_sw128(smem_u32(sK), 16, 1024);      // K-major A of S^T
+      const uint64_t dV = smem_desc_sw128(smem_u32(sV), 16, 1024);      // K-major A of dP^T
+      const uint64_t dKmn = smem_desc_sw128(smem_u32(sK), 8192, 1024);  // MN-major B of dQ
+      const uint64_t dQk = smem_desc_sw128(smem_u32(sQ), 16, 1024);     // K-major B of S^T (stage 0)
+      const uint64_t dOk = smem_desc_sw128(smem_u32(sO), 16, 1024);
+      const uint64_t dQmn = smem_desc_sw128(smem_u32(sQ), 8192, 1024);  // MN-major B of dK
+      const uint64_t dOmn = smem_desc_sw128(smem_u32(sO), 8192, 1024);  // MN-major B of dV
+      const uint64_t dSt = smem_desc_sw128(smem_u32(sSt), 16384, 1024); // MN-major A of dQ (buffer 0)
       // S^T / dP^T of query half hf of tile t: M 128 keys, N 64 queries, into TMEM columns
       // [64 hf, 64 hf + 64) and [128 + 64 hf, ...).
       auto issue_sdp = [&](int t, int hf) {
-        const uint32_t q_addr = smem_u32(sQ + (t & 1) * kTileBytes) + hf * 8192;
-        const uint32_t o_addr = smem_u32(sO + (t & 1) * kTileBytes) + hf * 8192;
+        const uint32_t off = (t & 1) * kTileBytes + hf * 8192;
+        const uint64_t bq = desc_adv(dQk, off), bo = desc_adv(dOk, off);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          umma_f16(tmem + hf * 64, smem_desc_sw128(k_addr + kk * 32, 16, 1024),
-                   smem_desc_sw128(q_addr + kk * 32, 16, 1024), id_sq, kk > 0 ? 1u : 0u);
-          umma_f16(tmem + 128 + hf * 64, smem_desc_sw128(v_addr + kk * 32, 16, 1024),
-                   smem_desc_sw128(o_addr + kk * 32, 16, 1024), id_sq, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + hf * 64, desc_adv(dK, kk * 32), desc_adv(bq, kk * 32), id_sq, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 128 + hf * 64, desc_adv(dV, kk * 32), desc_adv(bo, kk * 32), id_sq, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->sdp_full[hf]);
       };
@@ -594,7 +604,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       for (int t = 0; t < ntiles && ok; ++t) {
         const int s = t & 1;
-        const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), o_addr = smem_u32(sO + s * kTileBytes);
+        const uint64_t bq = desc_adv(dQmn, s * kTileBytes), bo = desc_adv(dOmn, s * kTileBytes);
         for (int hf = 0; hf < 2 && ok; ++hf) {
           // P^T / dS^T of this half are in TMEM (over its S^T / dP^T columns).
           if (!(ok = wait(&bars->p_full[hf], t & 1, abort_flag, status, kFaMma))) break;
@@ -603,9 +613,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int j = 0; j < 4; ++j) {
             const int kk = hf * 4 + j;  // 16 queries per step
             const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-            umma_f16_ts(tmem + 256, tmem + pair_col(kk), smem_desc_sw128(o_addr + kk * 2048, 8192, 1024), id_kn, acc);
-            umma_f16_ts(tmem + 320, tmem + 128 + pair_col(kk), smem_desc_sw128(q_addr + kk * 2048, 8192, 1024), id_kn,
-                        acc);
+            umma_f16_ts(tmem + 256, tmem + pair_col(kk), desc_adv(bo, kk * 2048), id_kn, acc);
+            umma_f16_ts(tmem + 320, tmem + 128 + pair_col(kk), desc_adv(bq, kk * 2048), id_kn, acc);
           }
           if (hf == 1) umma_commit(&bars->q_empty[s]);  // Q_t / dO_t are no longer read
           // The next tile's scores of this half overwrite the columns dV / dK just read; the
@@ -619,12 +628,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!ok) break;
         if (!(ok = wait(&bars->dq_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, status, kFaMma))) break;
         tc_fence_after();
-        const uint32_t sbuf = st_addr + s * kPBytes;
+        const uint64_t sbuf = desc_adv(dSt, s * kPBytes);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
           // dS^T read MN-major: queries contiguous (two 64-query halves 16 KiB apart), 16 keys per step.
-          umma_f16(tmem + 384 + (t & 1) * D, smem_desc_sw128(sbuf + kk * 2048, 16384, 1024),
-                   smem_desc_sw128(k_addr + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 384 + (t & 1) * D, desc_adv(sbuf, kk * 2048), desc_adv(dKmn, kk * 2048), id_q,
+                   kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->grads_done);
       }

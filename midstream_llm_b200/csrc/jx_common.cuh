@@ -262,6 +262,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// The descriptor of the same layout `bytes` further on: the start address is the low
+// 14-bit field (address >> 4) and shared memory addresses stay below 2^18, so the
+// addition never carries into the next field.
+__device__ __forceinline__ uint64_t desc_adv(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
+
 // Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A/B fp16 (formats 0),
 // A/B major at bits 15/16 (1 = MN-major), N>>3 at [17,23), M>>4 at [24,29).
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool a_mn_major, bool b_mn_major) {
