@@ -73,6 +73,18 @@ int jx_rmsnorm_bwd(const void* dy, const void* x, const float* rstd, const float
 /* dgamma (+)= sum over parts (accumulate != 0 adds to the existing value). */
 int jx_rmsnorm_dgamma_reduce(const float* dgamma_part, int nparts, int cols, float* dgamma, int accumulate,
                              jx_stream_t stream);
+/* ---- LayerNorm (model_torch.py:12-15, norm_type "layernorm"; fp32 under autocast) ----
+ * y = f16((x - mean) * rstd * gamma + beta) with fp32 statistics of the f16 row x
+ * (biased variance, rstd = 1/sqrt(var + eps)); beta may be NULL (norm_bias false).
+ * mean, rstd: f32 [rows], saved for the backward. cols: multiple of 8, <= 4096. */
+int jx_layernorm_fwd(const void* x, const float* gamma, const float* beta, void* y, float* mean, float* rstd,
+                     int64_t rows, int cols, float eps, jx_stream_t stream);
+/* dx = f16(f16(layer-norm input gradient in fp32) + dresid) (dresid may be NULL);
+ * dgamma_part / dbeta_part: f32 [nparts, cols], nparts = jx_rmsnorm_bwd_parts(rows),
+ * reduced with jx_rmsnorm_dgamma_reduce; dbeta_part may be NULL. */
+int jx_layernorm_bwd(const void* dy, const void* x, const float* mean, const float* rstd, const float* gamma,
+                     const void* dresid, void* dx, float* dgamma_part, float* dbeta_part, int64_t rows, int cols,
+                     jx_stream_t stream);
 /* RMSNorm backward that allocates nothing and needs no scratch from the caller:
  * for callers that cannot allocate device memory (a runtime bound through this
  * C ABI without a device allocator of its own, or one held to a fixed memory

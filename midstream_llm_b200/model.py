@@ -11,7 +11,8 @@ Mirrors Midstream-LLM src/jishui/model_torch.py:
 
 Numerics follow the reference's fp16 autocast recipe (pretrain_torch.py:212):
 fp32 master weights, fp16 GEMM operands with fp32 accumulation, fp16 residual
-stream, fp32 RMSNorm statistics / RoPE / softmax / CE. The B200 path always
+stream, fp32 norm statistics (RMSNorm, or LayerNorm run in fp32 as autocast runs it) /
+RoPE / softmax / CE. The B200 path always
 computes this recipe (there is no fp32 or CPU path); it raises if the
 configuration is outside what the kernels implement.
 
@@ -74,8 +75,6 @@ def rope_tables(seq_len: int, head_dim: int, theta: float, device) -> tuple[torc
 def check_supported(config: ModelConfig) -> None:
     """Raises for configurations the sm_100a kernels do not implement (no silent fallback)."""
     problems = []
-    if config.norm_type != "rmsnorm":
-        problems.append("norm_type must be 'rmsnorm' (LayerNorm kernels are not built)")
     if config.attention_bias or config.mlp_bias:
         problems.append("attention_bias / mlp_bias are not supported")
     if not config.tie_word_embeddings:
@@ -91,6 +90,13 @@ def check_supported(config: ModelConfig) -> None:
 
 
 # --------------------------------------------------------------------------- module tree
+def make_norm(config: ModelConfig) -> nn.Module:
+    """The reference's norm choice (model_torch.py:12-15): RMSNorm, or LayerNorm with optional bias."""
+    if config.norm_type == "rmsnorm":
+        return nn.RMSNorm(config.hidden_size, eps=config.norm_eps)
+    return nn.LayerNorm(config.hidden_size, eps=config.norm_eps, bias=config.norm_bias)
+
+
 class CausalSelfAttention(nn.Module):
     def __init__(self, config: ModelConfig):
         super().__init__()
@@ -115,9 +121,9 @@ class SwiGLU(nn.Module):
 class TransformerBlock(nn.Module):
     def __init__(self, config: ModelConfig):
         super().__init__()
-        self.input_norm = nn.RMSNorm(config.hidden_size, eps=config.norm_eps)
+        self.input_norm = make_norm(config)
         self.attention = CausalSelfAttention(config)
-        self.post_attention_norm = nn.RMSNorm(config.hidden_size, eps=config.norm_eps)
+        self.post_attention_norm = make_norm(config)
         self.mlp = SwiGLU(config)
 
 
@@ -213,12 +219,14 @@ class FlatParams:
 @dataclass
 class LayerActs:
     h1: torch.Tensor
+    mean1: torch.Tensor               # LayerNorm only (unused for RMSNorm)
     rstd1: torch.Tensor
     qkv: torch.Tensor
     o: torch.Tensor
     lse: torch.Tensor
     xmid: torch.Tensor
     h2: torch.Tensor
+    mean2: torch.Tensor
     rstd2: torch.Tensor
     gate: torch.Tensor
     up: torch.Tensor
@@ -232,6 +240,7 @@ class Workspace:
     xs: torch.Tensor                  # [L+1, M, d] residual stream at every layer boundary
     acts: list[LayerActs]             # per layer, or a single recompute slot under checkpointing
     hf: torch.Tensor
+    meanf: torch.Tensor
     rstdf: torch.Tensor
     logits: torch.Tensor              # [M, V] fp16; overwritten in place by dlogits in backward
     ce_lse: torch.Tensor
@@ -278,7 +287,7 @@ class JishuiForCausalLM(nn.Module):
         self.config = config
         self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
         self.layers = nn.ModuleList([TransformerBlock(config) for _ in range(config.num_hidden_layers)])
-        self.norm = nn.RMSNorm(config.hidden_size, eps=config.norm_eps)
+        self.norm = make_norm(config)
         self._flat: FlatParams | None = None
         self._ws: dict = {}
         self._gen = 0
@@ -311,9 +320,10 @@ class JishuiForCausalLM(nn.Module):
         nslots = 1 if (not train or c.gradient_checkpointing) else L
 
         def acts():
-            return LayerActs(h1=torch.empty(M, d, **f16), rstd1=torch.empty(M, **f32), qkv=torch.empty(M, 3 * d, **f16),
+            return LayerActs(h1=torch.empty(M, d, **f16), mean1=torch.empty(M, **f32), rstd1=torch.empty(M, **f32),
+                             qkv=torch.empty(M, 3 * d, **f16),
                              o=torch.empty(M, d, **f16), lse=torch.empty(B, H, T, **f32), xmid=torch.empty(M, d, **f16),
-                             h2=torch.empty(M, d, **f16), rstd2=torch.empty(M, **f32),
+                             h2=torch.empty(M, d, **f16), mean2=torch.empty(M, **f32), rstd2=torch.empty(M, **f32),
                              gate=torch.empty(M, F, **f16), up=torch.empty(M, F, **f16), act=torch.empty(M, F, **f16))
 
         cos, sin = rope_tables(T, c.head_dim, c.rope_theta, dev)
@@ -326,14 +336,14 @@ class JishuiForCausalLM(nn.Module):
         xs_slots = L + 1 if train else 2
         ws = Workspace(
             B=B, T=T, xs=torch.empty(xs_slots, M, d, **f16), acts=[acts() for _ in range(nslots)],
-            hf=torch.empty(M, d, **f16), rstdf=torch.empty(M, **f32), logits=torch.empty(M, c.vocab_size, **f16),
+            hf=torch.empty(M, d, **f16), meanf=torch.empty(M, **f32), rstdf=torch.empty(M, **f32), logits=torch.empty(M, c.vocab_size, **f16),
             ce_lse=torch.empty(M, **f32), row_loss=torch.empty(M, **f32),
             dx=torch.empty(M, d, **f16) if train else None, dxmid=torch.empty(M, d, **f16) if train else None,
             dh=torch.empty(M, d, **f16) if train else None, do=torch.empty(M, d, **f16) if train else None,
             dqkv=torch.empty(M, 3 * d, **f16) if train else None, dgu=torch.empty(M, 2 * F, **f16) if train else None,
             attn_ws=torch.empty(ops.attn_bwd_workspace_bytes(B, T, H, c.head_dim) // 4 + 4, **f32) if train else None,
             attn_fwd_ws=torch.empty(ops.attn_fwd_workspace_bytes(B, T, H, c.head_dim) // 4 + 4, **f32),
-            norm_part=torch.empty(nparts * d, **f32), wgrad_ws=torch.empty(max(wmax // 4, 4), **f32),
+            norm_part=torch.empty(2 * nparts * d, **f32), wgrad_ws=torch.empty(max(wmax // 4, 4), **f32),
             cos=cos, sin=sin)
         self._ws[key] = ws
         return ws
@@ -356,19 +366,44 @@ class JishuiForCausalLM(nn.Module):
             gqkv=fl.g32_rows(q, 3 * d, d), go=fl.g32_rows(pre + "attention.o_proj.weight", d, d),
             ggu=fl.g32_rows(g, 2 * F, d), gd=fl.g32_rows(pre + "mlp.down_proj.weight", d, F),
             gg1=fl.g32_view(pre + "input_norm.weight", (d,)), gg2=fl.g32_view(pre + "post_attention_norm.weight", (d,)),
+            b1=self._bias_view(fl.p32_view, pre + "input_norm.bias"),
+            b2=self._bias_view(fl.p32_view, pre + "post_attention_norm.bias"),
+            gb1=self._bias_view(fl.g32_view, pre + "input_norm.bias"),
+            gb2=self._bias_view(fl.g32_view, pre + "post_attention_norm.bias"),
             lo=fl.offsets[pre + "input_norm.weight"],
             hi=fl.offsets[pre + "mlp.down_proj.weight"] + _round_up(d * F))
+
+    def _bias_view(self, view, name: str):
+        """fp32 view of a LayerNorm bias (None when the configuration has none)."""
+        if self.config.norm_type == "rmsnorm" or not self.config.norm_bias:
+            return None
+        return view(name, (self.config.hidden_size,))
+
+    # ---- norm dispatch (RMSNorm or LayerNorm, model_torch.py:12-15) ------------
+    def _norm_fwd(self, x, gamma, beta, out, mean, rstd) -> None:
+        c = self.config
+        if c.norm_type == "rmsnorm":
+            ops.rmsnorm_fwd(x, gamma, c.norm_eps, out=out, rstd=rstd)
+        else:
+            ops.layernorm_fwd(x, gamma, beta, c.norm_eps, out=out, mean=mean, rstd=rstd)
+
+    def _norm_bwd(self, dy, x, mean, rstd, gamma, dgamma, dbeta, acc, dresid, out, part) -> None:
+        if self.config.norm_type == "rmsnorm":
+            ops.rmsnorm_bwd(dy, x, rstd, gamma, dresid=dresid, out=out, dgamma=dgamma, accumulate=acc, part=part)
+        else:
+            ops.layernorm_bwd(dy, x, mean, rstd, gamma, dgamma=dgamma, dbeta=dbeta, accumulate=acc, dresid=dresid,
+                              out=out, part=part)
 
     # ---- forward pieces ------------------------------------------------------
     def _layer_fwd(self, w, ws: Workspace, x_in: torch.Tensor, x_out: torch.Tensor, A: LayerActs) -> None:
         c = self.config
         B, T = ws.B, ws.T
         d, F, H, hd = c.hidden_size, c.intermediate_size, c.num_attention_heads, c.head_dim
-        ops.rmsnorm_fwd(x_in, w["g1"], c.norm_eps, out=A.h1, rstd=A.rstd1)
+        self._norm_fwd(x_in, w["g1"], w["b1"], A.h1, A.mean1, A.rstd1)
         ops.gemm_qkv_rope(A.h1, w["wqkv"], d, ws.cos, ws.sin, T, hd, out=A.qkv)
         ops.attn_fwd(A.qkv, B, T, H, hd, out=A.o, lse=A.lse, workspace=ws.attn_fwd_ws)
         ops.gemm_f16(A.o, w["wo"], resid=x_in, out=A.xmid)
-        ops.rmsnorm_fwd(A.xmid, w["g2"], c.norm_eps, out=A.h2, rstd=A.rstd2)
+        self._norm_fwd(A.xmid, w["g2"], w["b2"], A.h2, A.mean2, A.rstd2)
         ops.gemm_swiglu_fwd(A.h2, w["wgu"], F, gate=A.gate, up=A.up, act=A.act)
         ops.gemm_f16(A.act, w["wd"], resid=A.xmid, out=x_out)
 
@@ -392,7 +427,8 @@ class JishuiForCausalLM(nn.Module):
             A = ws.acts[0 if (ckpt or not train) else i]
             self._layer_fwd(w, ws, x_in, x_out, A)
         x_last = ws.xs[c.num_hidden_layers] if train else ws.xs[c.num_hidden_layers % 2]
-        ops.rmsnorm_fwd(x_last, fl.p32_view("norm.weight", (c.hidden_size,)), c.norm_eps, out=ws.hf, rstd=ws.rstdf)
+        self._norm_fwd(x_last, fl.p32_view("norm.weight", (c.hidden_size,)), self._bias_view(fl.p32_view, "norm.bias"),
+                       ws.hf, ws.meanf, ws.rstdf)
         ops.gemm_f16(ws.hf, e16, out=ws.logits)
         ws.extra["x_last"] = x_last
         return ws
@@ -439,11 +475,13 @@ class JishuiForCausalLM(nn.Module):
         ops.gemm_f16(ws.logits, e16, b_mn_major=True, out=ws.dh)
         ops.gemm_wgrad(ws.logits, ws.hf, ge, accumulate, _wgrad_splits(V, d, ws.B * ws.T), ws.wgrad_ws)
         x_last = ws.extra["x_last"]
-        ops.rmsnorm_bwd(ws.dh, x_last, ws.rstdf, fl.p32_view("norm.weight", (d,)), out=ws.dx,
-                        dgamma=fl.g32_view("norm.weight", (d,)), accumulate=accumulate, part=ws.norm_part)
+        self._norm_bwd(ws.dh, x_last, ws.meanf, ws.rstdf, fl.p32_view("norm.weight", (d,)),
+                       fl.g32_view("norm.weight", (d,)), self._bias_view(fl.g32_view, "norm.bias"), accumulate, None,
+                       ws.dx, ws.norm_part)
         if reducer is not None:
             o = fl.offsets["norm.weight"]
-            reducer.ready(o, o + _round_up(d))
+            last = "norm.bias" if "norm.bias" in fl.offsets else "norm.weight"
+            reducer.ready(o, fl.offsets[last] + _round_up(d))
         ckpt = c.gradient_checkpointing
         for i in reversed(range(L)):
             w = self._layer_weights(fl, i)
@@ -468,15 +506,13 @@ class JishuiForCausalLM(nn.Module):
         ops.gemm_wgrad(ws.dx, A.act, w["gd"], acc, _wgrad_splits(d, F, M), ws.wgrad_ws)
         ops.gemm_f16(ws.dgu, w["wgu"], b_mn_major=True, out=ws.dh)
         ops.gemm_wgrad(ws.dgu, A.h2, w["ggu"], acc, _wgrad_splits(2 * F, d, M), ws.wgrad_ws)
-        ops.rmsnorm_bwd(ws.dh, A.xmid, A.rstd2, w["g2"], dresid=ws.dx, out=ws.dxmid, dgamma=w["gg2"], accumulate=acc,
-                        part=ws.norm_part)
+        self._norm_bwd(ws.dh, A.xmid, A.mean2, A.rstd2, w["g2"], w["gg2"], w["gb2"], acc, ws.dx, ws.dxmid, ws.norm_part)
         ops.gemm_f16(ws.dxmid, w["wo"], b_mn_major=True, out=ws.do)
         ops.gemm_wgrad(ws.dxmid, A.o, w["go"], acc, _wgrad_splits(d, d, M), ws.wgrad_ws)
         ops.attn_bwd(A.qkv, A.o, ws.do, A.lse, B, T, H, hd, cos=ws.cos, sin=ws.sin, out=ws.dqkv, workspace=ws.attn_ws)
         ops.gemm_f16(ws.dqkv, w["wqkv"], b_mn_major=True, out=ws.dh)
         ops.gemm_wgrad(ws.dqkv, A.h1, w["gqkv"], acc, _wgrad_splits(3 * d, d, M), ws.wgrad_ws)
-        ops.rmsnorm_bwd(ws.dh, x_in, A.rstd1, w["g1"], dresid=ws.dxmid, out=ws.dx, dgamma=w["gg1"], accumulate=acc,
-                        part=ws.norm_part)
+        self._norm_bwd(ws.dh, x_in, A.mean1, A.rstd1, w["g1"], w["gg1"], w["gb1"], acc, ws.dxmid, ws.dx, ws.norm_part)
 
 
 class _LossFn(torch.autograd.Function):

@@ -112,6 +112,53 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor, gamma: to
     return dx, dgamma
 
 
+def layernorm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor | None, eps: float,
+                  out: torch.Tensor | None = None, mean: torch.Tensor | None = None, rstd: torch.Tensor | None = None):
+    """LayerNorm in fp32 over fp16 rows, fp16 output: returns (y, mean, rstd)."""
+    _check(x, F16, "x")
+    _check(gamma, F32, "gamma")
+    if beta is not None:
+        _check(beta, F32, "beta")
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    y = out if out is not None else torch.empty_like(x)
+    mean = mean if mean is not None else torch.empty(rows, device=x.device, dtype=F32)
+    rstd = rstd if rstd is not None else torch.empty(rows, device=x.device, dtype=F32)
+    _lib.call("jx_layernorm_fwd", x.data_ptr(), gamma.data_ptr(), _ptr(beta), y.data_ptr(), mean.data_ptr(),
+              rstd.data_ptr(), rows, cols, float(eps), _stream())
+    return y, mean, rstd
+
+
+def layernorm_bwd(dy: torch.Tensor, x: torch.Tensor, mean: torch.Tensor, rstd: torch.Tensor, gamma: torch.Tensor,
+                  dgamma: torch.Tensor | None = None, dbeta: torch.Tensor | None = None, accumulate: bool = False,
+                  dresid: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                  part: torch.Tensor | None = None):
+    """Returns (dx, dgamma, dbeta); dgamma / dbeta are accumulated into when `accumulate` and given.
+    dbeta is computed only when a tensor is passed for it."""
+    _check(dy, F16, "dy")
+    _check(x, F16, "x")
+    _check(gamma, F32, "gamma")
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    dx = out if out is not None else torch.empty_like(x)
+    nparts = _lib.query("jx_rmsnorm_bwd_parts", rows)
+    if part is None or part.numel() < 2 * nparts * cols:
+        part = torch.empty(2 * nparts * cols, device=x.device, dtype=F32)
+    if dresid is not None:
+        _check(dresid, F16, "dresid")
+    pb = part[nparts * cols:] if dbeta is not None else None
+    _lib.call("jx_layernorm_bwd", dy.data_ptr(), x.data_ptr(), mean.data_ptr(), rstd.data_ptr(), gamma.data_ptr(),
+              _ptr(dresid), dx.data_ptr(), part.data_ptr(), _ptr(pb), rows, cols, _stream())
+    if dgamma is None:
+        dgamma = torch.empty(cols, device=x.device, dtype=F32)
+        accumulate = False
+    _lib.call("jx_rmsnorm_dgamma_reduce", part.data_ptr(), nparts, cols, dgamma.data_ptr(), int(accumulate), _stream())
+    if dbeta is not None:
+        _lib.call("jx_rmsnorm_dgamma_reduce", pb.data_ptr(), nparts, cols, dbeta.data_ptr(), int(accumulate),
+                  _stream())
+    return dx, dgamma, dbeta
+
+
 # ---------------------------------------------------------------- embedding
 def embed_fwd(ids: torch.Tensor, table16: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _check(ids, I64, "ids")

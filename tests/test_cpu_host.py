@@ -56,10 +56,26 @@ def test_model_refuses_cpu_forward_and_unsupported_configs():
     m = JishuiForCausalLM(jishui_tiny())
     with pytest.raises(RuntimeError, match="CUDA only"):
         m(torch.zeros(1, 8, dtype=torch.long))
-    for bad in (dict(norm_type="layernorm"), dict(num_key_value_heads=2), dict(attention_bias=True),
-                dict(tie_word_embeddings=False)):
+    for bad in (dict(num_key_value_heads=2), dict(attention_bias=True), dict(tie_word_embeddings=False)):
         with pytest.raises(ValueError, match="unsupported"):
             JishuiForCausalLM(replace(jishui_tiny(), **bad))
+
+
+def test_layernorm_model_has_reference_parameter_names():
+    """LayerNorm configurations build the reference's module tree (model_torch.py:12-15): weight and bias per
+    norm, in named_parameters() order, so state dicts move both ways."""
+    import sys
+    sys.path.insert(0, str(ROOT))
+    from oracle import jishui_ref as oracle
+    from midstream_llm_b200 import JishuiForCausalLM
+    from midstream_llm_b200.config import jishui_tiny
+    for bias in (True, False):
+        cfg = replace(jishui_tiny(), norm_type="layernorm", norm_bias=bias)
+        ref, mine = oracle.JishuiRef(cfg), JishuiForCausalLM(cfg)
+        names = [(n, tuple(p.shape)) for n, p in mine.named_parameters()]
+        assert names == [(n, tuple(p.shape)) for n, p in ref.named_parameters()]
+        assert ("norm.bias", (cfg.hidden_size,)) in names if bias else all("bias" not in n for n, _ in names)
+        mine.load_state_dict(ref.state_dict(), strict=True)
 
 
 def test_config_validation_matches_reference_rules():

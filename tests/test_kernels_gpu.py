@@ -139,6 +139,33 @@ def test_rmsnorm(ops, with_resid):
     assert rel_err(dg, gf.grad) < TOL
 
 
+@pytest.mark.parametrize("cols,bias,with_resid", [(704, True, True), (1024, False, False), (2112, True, False)])
+def test_layernorm(ops, cols, bias, with_resid):
+    """LayerNorm as autocast runs it: fp32 layer_norm of the widened fp16 input, fp16 output;
+    backward in fp32, input gradient rounded to fp16 and added to the fp16 residual gradient."""
+    rows = 1000
+    x = _h(rows, cols, seed=40) + 0.5
+    gamma = (1 + 0.1 * torch.randn(cols, device="cuda")).float()
+    beta = (0.1 * torch.randn(cols, device="cuda")).float() if bias else None
+    y, mean, rstd = ops.layernorm_fwd(x, gamma, beta, 1e-5)
+    xf = x.float().requires_grad_(True)
+    gf = gamma.clone().requires_grad_(True)
+    bf = beta.clone().requires_grad_(True) if bias else None
+    yr = torch.nn.functional.layer_norm(xf, (cols,), gf, bf, 1e-5)
+    assert rel_err(y, yr) < TOL
+    assert rel_err(mean, x.float().mean(-1)) < 1e-5
+    dy = _h(rows, cols, seed=41)
+    dres = _h(rows, cols, seed=42) if with_resid else None
+    dbeta = torch.zeros(cols, device="cuda") if bias else None
+    dx, dg, db = ops.layernorm_bwd(dy, x, mean, rstd, gamma, dbeta=dbeta, dresid=dres)
+    yr.backward(dy.float())
+    ref_dx = xf.grad.half().float() + (dres.float() if with_resid else 0)
+    assert rel_err(dx, ref_dx) < TOL
+    assert rel_err(dg, gf.grad) < TOL
+    if bias:
+        assert rel_err(db, bf.grad) < TOL
+
+
 def test_embedding(ops):
     V, d, n = 1000, 256, 4096
     table = torch.randn(V, d, device="cuda")
