@@ -51,7 +51,18 @@ def workload(name: str, n_gpus: int) -> dict:
         return dict(name="jishui-200m-seq1024", seq=1024, micro=16, accum=4 if n_gpus == 1 else 1, ckpt=False)
     if name == "long":
         return dict(name="jishui-200m-seq4096-recompute", seq=4096, micro=4, accum=1, ckpt=True)
+    if name == "base":
+        # The reference's production run (configs/jishui-200m-cuda-4b.json): 16,384 tokens per update
+        # (batch 1 x accum 8 there; one micro-batch of 8 x 2048 here, the same update).
+        return dict(name="jishui-200m-base-layernorm-seq2048", seq=2048, micro=8, accum=1, ckpt=False, cfg="base")
     raise SystemExit(f"unknown workload {name}")
+
+
+def workload_config(wl: dict):
+    from midstream_llm_b200.config import jishui_200m, jishui_200m_base
+    if wl.get("cfg") == "base":
+        return jishui_200m_base(wl["ckpt"])
+    return jishui_200m(wl["seq"], gradient_checkpointing=wl["ckpt"])
 
 
 def model_flops_per_token(cfg, seq: int) -> tuple[float, float]:
@@ -65,11 +76,11 @@ def init_weights(model, seed: int) -> None:
     """N(0, 0.02) for every 2-D parameter in named_parameters() order, gains 1."""
     gen = torch.Generator().manual_seed(seed)
     with torch.no_grad():
-        for _, p in model.named_parameters():
+        for name, p in model.named_parameters():
             if p.dim() == 2:
                 p.copy_(torch.randn(p.shape, generator=gen) * 0.02)
             else:
-                p.fill_(1.0)
+                p.fill_(0.0 if name.endswith(".bias") else 1.0)
 
 
 class ClockSampler:
@@ -127,14 +138,14 @@ class ClockSampler:
                 "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
-def cpu_reference_rate(steps: int, warmup: int, seq: int, seed: int = 0) -> dict:
+def cpu_reference_rate(steps: int, warmup: int, seq: int, cfg, seed: int = 0) -> dict:
     """The reference update (oracle restatement, fp32, no autocast) on the host cores:
-    the 200M model at micro-batch 1 x seq, tokens/s over `steps` updates."""
+    the workload's model at micro-batch 1 x seq, tokens/s over `steps` updates."""
     from oracle import jishui_ref as oracle
-    from midstream_llm_b200.config import jishui_200m
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cfg = jishui_200m(seq)
+    from dataclasses import replace
+    cfg = replace(cfg, gradient_checkpointing=False)
     torch.manual_seed(seed)
     model = oracle.JishuiRef(cfg)
     oracle.init_weights(model, seed)
@@ -148,7 +159,7 @@ def cpu_reference_rate(steps: int, warmup: int, seq: int, seed: int = 0) -> dict
         oracle.reference_update(model, opt, None, lambda: batch, 1, 1.0, 3e-4, device_type="cpu")
     dt = time.perf_counter() - t0
     return {"value": steps * seq / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} fp32 updates of the 200M model at micro-batch 1x{seq} on {threads} host threads "
+            "sample": f"{steps} fp32 updates of {cfg.name} at micro-batch 1x{seq} on {threads} host threads "
                       f"(oracle restatement of model_torch + pretrain_torch update, no autocast)"}
 
 
@@ -157,10 +168,9 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     wl = workload(args.workload, args.gpus)
-    from midstream_llm_b200.config import jishui_200m
-    cfg = jishui_200m(wl["seq"])
+    cfg = workload_config(wl)
     steps = max(1, min(args.steps, 3))
-    base = cpu_reference_rate(steps, min(args.warmup, 1), wl["seq"])
+    base = cpu_reference_rate(steps, min(args.warmup, 1), wl["seq"], cfg)
     f_model, _ = model_flops_per_token(cfg, wl["seq"])
     line = {"metric": "train tokens/s", "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": 1000.0 * wl["seq"] / base["value"],
@@ -181,7 +191,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--workload", choices=("200m", "long"), default="200m")
+    ap.add_argument("--workload", choices=("200m", "long", "base"), default="200m")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -193,7 +203,6 @@ def main() -> None:
 
     import torch.distributed as dist
     from midstream_llm_b200 import AdamW, GradScaler, JishuiForCausalLM, _lib, ops, train_update
-    from midstream_llm_b200.config import jishui_200m
     from midstream_llm_b200.data import ZipfBatches
     from midstream_llm_b200.distributed import GradReducer, LaunchEnvironment, build_runtime_plan, initialize_runtime
 
@@ -205,7 +214,7 @@ def main() -> None:
     rank, world = env.rank, env.world_size
     wl = workload(args.workload, world)
     B, T, accum = wl["micro"], wl["seq"], wl["accum"]
-    cfg = jishui_200m(T, gradient_checkpointing=wl["ckpt"])
+    cfg = workload_config(wl)
 
     model = JishuiForCausalLM(cfg)
     init_weights(model, seed=0)  # identical on every rank
@@ -288,14 +297,15 @@ def main() -> None:
             traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
         cpu = None
         if not args.no_cpu_baseline and world == 1:
-            cpu = cpu_reference_rate(2, 1, T)
+            cpu = cpu_reference_rate(2, 1, T, cfg)
         line = {
             "metric": "train tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (Zipf 1.1 tokens, N(0,0.02) weights)",
             "config": {"workload": wl["name"], "model": cfg.name, "global_batch": B * accum * world, "micro_batch": B,
                        "grad_accum": accum, "seq_len": T, "parallelism": f"dp{world}",
-                       "l2": "working set (activations, 953 MB fp32 grads) far exceeds the 126 MB L2"},
+                       "l2": f"working set (activations, {4 * sum(p.numel() for p in model.parameters()) / 1e6:.0f} MB "
+                             "fp32 grads) far exceeds the 126 MB L2"},
             "mfu": value * f_model / (world * pk["bf16_tflops"] * 1e12),
             "mfu_palm": value * f_palm / (world * pk["bf16_tflops"] * 1e12),
             "peak_kind": pk_kind,

@@ -125,6 +125,16 @@ def jishui_200m(seq_len: int = 1024, gradient_checkpointing: bool = False) -> Mo
                        gradient_checkpointing=gradient_checkpointing)
 
 
+def jishui_200m_base(gradient_checkpointing: bool = False) -> ModelConfig:
+    """The reference's production decoder (configs/jishui-200m-cuda-4b.json): V 32768, d 704, 30 layers x 11
+    heads of 64, SwiGLU 1856, LayerNorm with bias, RoPE 10000, context 2048, tied embeddings."""
+    return ModelConfig(name="Jishui-200M-Base", vocab_size=32768, hidden_size=704, num_hidden_layers=30,
+                       num_attention_heads=11, num_key_value_heads=11, head_dim=64, intermediate_size=1856,
+                       norm_type="layernorm", norm_eps=1e-5, norm_bias=True, rope_theta=10000.0,
+                       max_position_embeddings=2048, tie_word_embeddings=True,
+                       gradient_checkpointing=gradient_checkpointing)
+
+
 def jishui_tiny(gradient_checkpointing: bool = False) -> ModelConfig:
     """Tiny debug decoder: V 24000, d 256, 4 layers x 4 heads of 64, SwiGLU 688."""
     return ModelConfig(name="jishui-tiny", vocab_size=24000, hidden_size=256, num_hidden_layers=4,
