@@ -10,8 +10,8 @@ from .config import ModelConfig, TrainConfig, jishui_200m, jishui_tiny, load_run
 from .model import JishuiForCausalLM, causal_lm_loss
 from .optim import AdamW, GradScaler, clip_grad_norm_
 from .schedules import continuation_lr, make_continuation_schedule
-from .trainer import train_update
+from .trainer import evaluate, train_update, validation_report
 
 __all__ = ["ModelConfig", "TrainConfig", "jishui_200m", "jishui_tiny", "load_run_config", "JishuiForCausalLM",
            "causal_lm_loss", "AdamW", "GradScaler", "clip_grad_norm_", "continuation_lr",
-           "make_continuation_schedule", "train_update"]
+           "make_continuation_schedule", "train_update", "evaluate", "validation_report"]

@@ -35,8 +35,9 @@ class ZipfBatches:
 
 
 def tensor_batch(rows: np.ndarray, device, pinned: bool = True):
-    """(inputs, targets) on `device` from [B, T+1] rows (pretrain_torch.py:38-40)."""
-    t = torch.from_numpy(rows)
+    """(inputs, targets) on `device` from [B, T+1] integer rows (any integer dtype, widened to int64 as
+    pretrain_torch.py:38-40 does)."""
+    t = torch.from_numpy(np.ascontiguousarray(rows, dtype=np.int64))
     if pinned and torch.device(device).type == "cuda":
         t = t.pin_memory()
     t = t.to(device, non_blocking=True)

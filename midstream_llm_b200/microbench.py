@@ -14,6 +14,7 @@ Shapes (the operator workload of the Jishui-200M step):
            step with 1 % +inf gradients runs the statistics pass only (2 B/param)
   gemm     the decoder's GEMM shapes with their fused epilogues
   attn     causal flash attention fwd / bwd at (B 16, T 1024) and (B 4, T 4096), 16 heads x 64
+  eval     validation forward (no autograd, fused head + CE) of the 200M model at 16 x 1024
 Each line is JSON with the time per call (CUDA events, after warm-up, inputs
 larger than L2 unless noted) and the achieved rate against the measured peaks.
 """
@@ -208,14 +209,37 @@ def bench_attn(iters: int) -> None:
               2.5 * fl, "TFLOP/s", pk.get("bf16_tflops", 1590.0))
 
 
+def bench_eval(iters: int) -> None:
+    """Validation forward (pretrain_torch.py:42-58): no autograd, fused head + CE, 200M model, 16 x 1024."""
+    from .config import jishui_200m
+    from .data import ZipfBatches
+    from .model import JishuiForCausalLM
+    pk = _peaks()
+    cfg = jishui_200m(1024)
+    torch.manual_seed(0)
+    model = JishuiForCausalLM(cfg).cuda()
+    with torch.no_grad():
+        for p in model.parameters():
+            if p.dim() == 2:
+                p.normal_(0.0, 0.02)
+    rows = torch.from_numpy(ZipfBatches(cfg.vocab_size, 16, 1024, seed=7).next_rows()).cuda()
+    x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
+    d, F, V, L = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size, cfg.num_hidden_layers
+    fwd_flops = 2.0 * 16 * 1024 * (L * (4 * d * d + 3 * d * F) + V * d) + 2.0 * L * 16 * 16 * 1024 * 1024 * 64
+    with torch.no_grad():
+        t = _time(lambda: model.loss(x, y), iters)
+    _emit("eval forward+CE 200M B16 T1024 (tokens/s: %.0f)" % (16 * 1024 / t), t, fwd_flops, "TFLOP/s",
+          pk.get("bf16_tflops", 1590.0))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--op", default="all", choices=("all", "rmsnorm", "ce", "adamw", "gemm", "attn"))
+    ap.add_argument("--op", default="all", choices=("all", "rmsnorm", "ce", "adamw", "gemm", "attn", "eval"))
     ap.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
     torch.cuda.set_device(0)
     for name, fn in (("rmsnorm", bench_rmsnorm), ("ce", bench_ce), ("adamw", bench_adamw), ("gemm", bench_gemm),
-                     ("attn", bench_attn)):
+                     ("attn", bench_attn), ("eval", bench_eval)):
         if a.op in ("all", name):
             fn(a.iters)
             torch.cuda.empty_cache()

@@ -20,6 +20,7 @@ from typing import Callable, Sequence
 
 import torch
 
+from .data import tensor_batch
 from .model import JishuiForCausalLM, causal_lm_loss
 from .optim import AdamW, GradScaler, clip_grad_norm_
 
@@ -62,3 +63,33 @@ def train_update(model: JishuiForCausalLM, optimizer: AdamW, scaler: GradScaler,
         scaler.update()
         return {"loss": loss_sum / grad_accum_steps, "grad_norm": norm, "attempts": attempt + 1, "lr": lr}
     raise FloatingPointError("gradient overflow persisted after 8 retries")
+
+
+@torch.no_grad()
+def evaluate(model: JishuiForCausalLM, iterator, eval_batches: int, device) -> float:
+    """Mean validation loss over `eval_batches` batches of `iterator` (any object whose next() returns
+    [B, T+1] integer rows, like the reference's SequentialBatchIterator), as pretrain_torch.py:42-58:
+    eval mode, no autograd, the fp16 recipe, mean of the per-batch mean losses, train mode restored,
+    FloatingPointError on a non-finite result. The per-batch losses are summed on the device in float64
+    and read once (the reference reads each one)."""
+    if eval_batches <= 0:
+        raise ValueError("eval_batches must be positive")
+    model.eval()
+    total = torch.zeros((), dtype=torch.float64, device=device)
+    for _ in range(eval_batches):
+        x, y = tensor_batch(next(iterator), device)
+        total += causal_lm_loss(model, x, y).double()
+    model.train()
+    result = float(total) / eval_batches
+    if not math.isfinite(result):
+        raise FloatingPointError("non-finite validation loss")
+    return result
+
+
+def validation_report(model: JishuiForCausalLM, make_iterator: Callable, eval_batches: int, device, step: int,
+                      categories: Sequence[int] = ()) -> dict:
+    """Overall and per-category validation loss (pretrain_torch.py:61-69): `make_iterator(category)` returns
+    a fresh validation iterator (category None = all); `categories` lists those present in the split."""
+    overall = evaluate(model, make_iterator(None), eval_batches, device)
+    per_category = {c: evaluate(model, make_iterator(c), eval_batches, device) for c in categories}
+    return {"step": step, "loss": overall, "per_category_loss": per_category}

@@ -184,3 +184,35 @@ def test_product_does_not_import_the_oracle():
     for path in (ROOT / "midstream_llm_b200").rglob("*.py"):
         text = path.read_text()
         assert "import oracle" not in text and "from oracle" not in text, path
+
+
+def test_evaluate_host_logic():
+    """evaluate(): mean of per-batch losses over eval_batches rows of the iterator, train mode restored, a
+    non-finite mean raises (pretrain_torch.py:42-58); validation_report() asks for one iterator per category."""
+    from midstream_llm_b200.trainer import evaluate, validation_report
+
+    class Stub(torch.nn.Module):
+        def __init__(self, values):
+            super().__init__()
+            self.values, self.seen = list(values), []
+
+        def loss(self, x, y):
+            assert not self.training and not torch.is_grad_enabled()
+            assert x.dtype == torch.int64 and x.shape == (2, 8) and torch.equal(x[:, 1:], y[:, :-1])
+            self.seen.append(int(x[0, 0]))
+            return torch.tensor(self.values.pop(0))
+
+    rows = (np.arange(5 * 2 * 9, dtype=np.uint16).reshape(5, 2, 9))
+    m = Stub([1.0, 2.0, 4.0])
+    assert evaluate(m, iter(rows), 3, "cpu") == pytest.approx(7.0 / 3)
+    assert m.training and m.seen == [0, 18, 36]
+    with pytest.raises(FloatingPointError, match="non-finite"):
+        evaluate(Stub([1.0, float("inf")]), iter(rows), 2, "cpu")
+    asked = []
+
+    def make(c):
+        asked.append(c)
+        return iter(rows)
+
+    rep = validation_report(Stub([1.0] * 3), make, 1, "cpu", step=200, categories=(2, 5))
+    assert asked == [None, 2, 5] and rep == {"step": 200, "loss": 1.0, "per_category_loss": {2: 1.0, 5: 1.0}}

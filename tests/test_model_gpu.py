@@ -240,3 +240,22 @@ def test_layernorm_model_parity(kw, B, T):
         e = rel_err(pm.grad, pr.grad)
         bound = max(1e-2, 1.5 * rel_err(p32.grad, pr.grad))
         assert e < bound, (n, e, bound)
+
+
+def test_evaluate_matches_reference_recipe():
+    """evaluate() against the reference's evaluate body (no_grad + fp16 autocast causal_lm_loss, mean of the
+    per-batch losses) on the same rows; no parameter gradient is created."""
+    import numpy as np
+    from midstream_llm_b200.trainer import evaluate
+    cfg = _cfg()
+    ref, mine = _pair(cfg)
+    rows = [oracle.zipf_tokens(cfg.vocab_size, 2, 256, 50 + i).numpy().astype(np.uint16) for i in range(3)]
+    losses = []
+    with torch.no_grad():
+        for r in rows:
+            t = torch.as_tensor(r.astype(np.int64), device="cuda")
+            with torch.autocast("cuda", dtype=torch.float16):
+                losses.append(float(oracle.causal_lm_loss(ref, t[:, :-1], t[:, 1:])))
+    got = evaluate(mine, iter(rows), 3, "cuda")
+    assert abs(got - sum(losses) / 3) / (sum(losses) / 3) < 1e-3
+    assert mine.training and all(p.grad is None for p in mine.parameters())
