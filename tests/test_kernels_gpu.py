@@ -103,9 +103,9 @@ def test_swiglu_fwd_bwd(ops, gemm_mode):
     assert rel_err(dgu[:, F:], uf.grad) < TOL
 
 
-@pytest.mark.parametrize("splits", [1, 4])
-def test_wgrad(ops, gemm_mode, splits):
-    T, N, K = 2048, 1024, 512
+# (2048, 2112, 704): the production q/k/v weight gradient, partial tiles in both output dimensions.
+@pytest.mark.parametrize("splits,T,N,K", [(1, 2048, 1024, 512), (4, 2048, 1024, 512), (3, 2048, 2112, 704)])
+def test_wgrad(ops, gemm_mode, splits, T, N, K):
     dy, x = _h(T, N, seed=10), _h(T, K, seed=11)
     g = torch.randn(N, K, device="cuda")
     g0 = g.clone()
