@@ -169,6 +169,13 @@ int jx_attn_bwd(const void* qkv, const void* out, const void* dout, const float*
                 int B, int T, int H, int D, float scale, const float* rope_cos, const float* rope_sin,
                 jx_stream_t stream);
 
+/* ---- Packed corpus rows (data.py:233-379 row filling, pretrain_torch.py:38-40 widening) ----
+ * out: int64 [rows, width]. Row r is covered by runs[row_start[r] .. row_start[r+1]) (int64 triples
+ * dst column, src token index into `tokens` (uint16 [ntokens]) or -(eod + 1), count), sorted by dst.
+ * A column outside every run, or a src beyond ntokens, writes -1 and records a device status. */
+int jx_pack_rows(const void* tokens, int64_t ntokens, const int64_t* runs, const int32_t* row_start, int rows,
+                 int width, int64_t* out, jx_stream_t stream);
+
 /* ---- Cross-entropy over f16 logits (model_torch.py:102-104) ----
  * Per row: lse = log(sum exp(logit)), loss = lse - logit[target]; rows whose
  * target == ignore_index give loss 0 and are excluded from the mean. */
