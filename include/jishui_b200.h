@@ -169,6 +169,19 @@ int jx_attn_bwd(const void* qkv, const void* out, const void* dout, const float*
                 int B, int T, int H, int D, float scale, const float* rope_cos, const float* rope_sin,
                 jx_stream_t stream);
 
+/* ---- Incremental decoding (generate_torch.py:279-285 re-runs model(tokens)[0, -1]) ----
+ * Causal attention of one new token per sequence against a KV cache: qkv is the new token's
+ * projection row (q | k | v, RoPE applied; row b at qkv + b*ld_qkv), kcache / vcache hold
+ * positions 0 .. len-2 (row stride ld_cache, sequence stride cache_batch_stride); the new k / v are
+ * appended at position len-1. out: f16 [B, H*64] (row stride ld_out). workspace: caller scratch of
+ * jx_attn_decode_workspace_bytes(B, H, max_len) bytes with max_len >= len. head_dim must be 64.
+ * If len_dev is non-NULL the length is read from that device int (for CUDA-graph replays) and `len`
+ * is only its upper bound, which sets the grid. */
+int64_t jx_attn_decode_workspace_bytes(int B, int H, int max_len);
+int jx_attn_decode(const void* qkv, int64_t ld_qkv, void* kcache, void* vcache, int64_t ld_cache,
+                   int64_t cache_batch_stride, int B, int len, const int* len_dev, int H, int D, float scale,
+                   void* workspace, void* out, int64_t ld_out, jx_stream_t stream);
+
 /* ---- Packed corpus rows (data.py:233-379 row filling, pretrain_torch.py:38-40 widening) ----
  * out: int64 [rows, width]. Row r is covered by runs[row_start[r] .. row_start[r+1]) (int64 triples
  * dst column, src token index into `tokens` (uint16 [ntokens]) or -(eod + 1), count), sorted by dst.

@@ -24,6 +24,9 @@ _SIGNATURES: dict[str, tuple] = {
     "jx_rmsnorm_dgamma_reduce": (c_int, [_P, c_int, c_int, _P, c_int, _P]),
     "jx_layernorm_fwd": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, c_int, c_float, _P]),
     "jx_layernorm_bwd": (c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_int64, c_int, _P]),
+    "jx_attn_decode_workspace_bytes": (c_int64, [c_int, c_int, c_int]),
+    "jx_attn_decode": (c_int, [_P, c_int64, _P, _P, c_int64, c_int64, c_int, c_int, _P, c_int, c_int, c_float, _P,
+                               _P, c_int64, _P]),
     "jx_pack_rows": (c_int, [_P, c_int64, _P, _P, c_int, c_int, _P, _P]),
     "jx_rmsnorm_bwd_noalloc": (c_int, [_P, _P, _P, _P, _P, _P, _P, c_int, c_int64, c_int, _P]),
     "jx_embed_fwd": (c_int, [_P, c_int64, _P, c_int64, c_int, _P, _P]),

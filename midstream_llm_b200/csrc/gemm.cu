@@ -877,6 +877,122 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int splits, in
   }
 }
 
+// ---------------------------------------------------------------------------
+// Small-M products (M <= 8, A and B K-major): C[m][n] = sum_k A[m][k] B[n][k],
+// for incremental decoding. The tensor-core tiles are 128 rows high, so for a
+// handful of rows the product is a weight-bandwidth problem: every CTA streams
+// one pair of B rows with 16-byte loads (its warps and lanes split K),
+// accumulates in fp32 for all M rows of A (L1-resident), reduces across the CTA
+// and applies the same epilogue as the tiled kernel (fp16 rounding points
+// included). A pair is the
+// two rows an epilogue needs together: (2q, 2q+1) for the plain / residual
+// epilogue, the RoPE partners (64h + c, 64h + c + 32) for q/k/v, and the gate /
+// up rows (q, F + q) for SwiGLU.
+// ---------------------------------------------------------------------------
+constexpr int kGemvMaxM = 8;
+constexpr int kGemvWarps = 4;
+
+template <int EPI>
+__device__ __forceinline__ void gemv_pair_rows(const Params& p, int q, int& r0, int& r1) {
+  if constexpr (EPI == kRope) {
+    r0 = (q / 32) * 64 + (q % 32);
+    r1 = r0 + 32;
+  } else if constexpr (EPI == kSwigluF) {
+    r0 = q;
+    r1 = p.swiglu_F + q;
+  } else {
+    r0 = 2 * q;
+    r1 = 2 * q + 1;
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __half* __restrict__ A, int64_t lda,
+                                                               const __half* __restrict__ B, int64_t ldb, Params p) {
+  __shared__ float red[kGemvWarps][kGemvMaxM][2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int q = blockIdx.x;  // one pair of B rows per CTA, K split across its warps
+  int r0, r1;
+  gemv_pair_rows<EPI>(p, q, r0, r1);
+  float acc[kGemvMaxM][2];
+#pragma unroll
+  for (int m = 0; m < kGemvMaxM; ++m) acc[m][0] = acc[m][1] = 0.f;
+  const __half* b0 = B + (int64_t)r0 * ldb;
+  const __half* b1 = B + (int64_t)r1 * ldb;
+  for (int k = (warp * 32 + lane) * 8; k < p.K; k += kGemvWarps * 256) {
+    const uint4 u0 = __ldg(reinterpret_cast<const uint4*>(b0 + k));
+    const uint4 u1 = __ldg(reinterpret_cast<const uint4*>(b1 + k));
+    const __half2* w0 = reinterpret_cast<const __half2*>(&u0);
+    const __half2* w1 = reinterpret_cast<const __half2*>(&u1);
+#pragma unroll
+    for (int m = 0; m < kGemvMaxM; ++m) {
+      if (m >= p.M) break;
+      const uint4 ua = __ldg(reinterpret_cast<const uint4*>(A + (int64_t)m * lda + k));
+      const __half2* xa = reinterpret_cast<const __half2*>(&ua);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 x = __half22float2(xa[j]), f0 = __half22float2(w0[j]), f1 = __half22float2(w1[j]);
+        acc[m][0] = fmaf(x.x, f0.x, fmaf(x.y, f0.y, acc[m][0]));
+        acc[m][1] = fmaf(x.x, f1.x, fmaf(x.y, f1.y, acc[m][1]));
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kGemvMaxM; ++m) {
+    const float s0 = warp_sum(acc[m][0]), s1 = warp_sum(acc[m][1]);
+    if (lane == 0) {
+      red[warp][m][0] = s0;
+      red[warp][m][1] = s1;
+    }
+  }
+  __syncthreads();
+  const int m = threadIdx.x;  // thread m writes row m of the pair
+  if (m >= p.M) return;
+  float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+  for (int w = 0; w < kGemvWarps; ++w) {
+    t0 += red[w][m][0];
+    t1 += red[w][m][1];
+  }
+  float v0 = h2f_round(t0), v1 = h2f_round(t1);
+  if constexpr (EPI == kF16) {
+    if (p.resid) {
+      v0 += __half2float(p.resid[(int64_t)m * p.ld_resid + r0]);
+      v1 += __half2float(p.resid[(int64_t)m * p.ld_resid + r1]);
+    }
+    p.C[(int64_t)m * p.ldc + r0] = __float2half_rn(v0);
+    p.C[(int64_t)m * p.ldc + r1] = __float2half_rn(v1);
+  } else if constexpr (EPI == kRope) {
+    if (r0 < p.rope_cols) {
+      const int pos = p.rope_seq > 0 ? m % p.rope_seq : 0;
+      const int c = q % 32;
+      const float cc = __ldg(p.rope_cos + (int64_t)pos * 32 + c), ss = __ldg(p.rope_sin + (int64_t)pos * 32 + c);
+      const float a = __fsub_rn(__fmul_rn(v0, cc), __fmul_rn(v1, ss));
+      const float bb = __fadd_rn(__fmul_rn(v0, ss), __fmul_rn(v1, cc));
+      v0 = a;
+      v1 = bb;
+    }
+    p.C[(int64_t)m * p.ldc + r0] = __float2half_rn(v0);
+    p.C[(int64_t)m * p.ldc + r1] = __float2half_rn(v1);
+  } else {  // kSwigluF: v0 = gate, v1 = up
+    p.C[(int64_t)m * p.ld_out + q] = __float2half_rn(v0);
+    p.out1[(int64_t)m * p.ld_out + q] = __float2half_rn(v1);
+    p.out2[(int64_t)m * p.ld_out + q] = __float2half_rn(__fmul_rn(h2f_round(silu_f(v0)), v1));
+  }
+}
+
+template <int EPI>
+int launch_gemv(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p, int pairs, cudaStream_t s,
+                const char* name) {
+  JX_CHECK_ARG(A && B && aligned16(A) && aligned16(B) && lda % 8 == 0 && ldb % 8 == 0 && p.K % 8 == 0,
+               "%s: small-M operands must be 16-byte aligned with K, lda, ldb multiples of 8", name);
+  JX_CHECK_ARG(pairs > 0 && pairs <= 0x7fffffff, "%s: bad shape", name);
+  gemv_kernel<EPI><<<pairs, kGemvWarps * 32, 0, s>>>(static_cast<const __half*>(A), lda,
+                                                     static_cast<const __half*>(B), ldb, p);
+  JX_CHECK_LAUNCH(name);
+  return JX_OK;
+}
+
 }  // namespace gemm
 
 // ---------------------------------------------------------------------------
@@ -1047,6 +1163,8 @@ extern "C" int jx_gemm_f16(const void* A, int64_t lda, int a_mn_major, const voi
   p.resid = static_cast<const __half*>(resid);
   p.ld_resid = ld_resid;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (M <= kGemvMaxM && !a_mn_major && !b_mn_major && N % 2 == 0)
+    return launch_gemv<kF16>(A, lda, B, ldb, p, N / 2, s, "jx_gemm_f16");
   if (!a_mn_major && !b_mn_major) return launch<kF16, false, false>(A, lda, B, ldb, p, s, "jx_gemm_f16");
   if (!a_mn_major && b_mn_major) return launch<kF16, false, true>(A, lda, B, ldb, p, s, "jx_gemm_f16");
   if (a_mn_major && !b_mn_major) return launch<kF16, true, false>(A, lda, B, ldb, p, s, "jx_gemm_f16");
@@ -1067,6 +1185,9 @@ extern "C" int jx_gemm_qkv_rope(const void* X, int64_t ldx, const void* W, int M
   p.rope_sin = rope_sin;
   p.rope_seq = seq_len;
   p.rope_cols = 2 * hidden;
+  if (M <= kGemvMaxM)
+    return launch_gemv<kRope>(X, ldx, W, K, p, 3 * hidden / 2, reinterpret_cast<cudaStream_t>(stream),
+                              "jx_gemm_qkv_rope");
   return launch<kRope, false, false>(X, ldx, W, K, p, reinterpret_cast<cudaStream_t>(stream), "jx_gemm_qkv_rope");
 }
 
@@ -1081,6 +1202,8 @@ extern "C" int jx_gemm_swiglu_fwd(const void* X, int64_t ldx, const void* Wgu, i
   p.out1 = static_cast<__half*>(up);
   p.out2 = static_cast<__half*>(act);
   p.ld_out = ld_out;
+  if (M <= kGemvMaxM)
+    return launch_gemv<kSwigluF>(X, ldx, Wgu, K, p, F, reinterpret_cast<cudaStream_t>(stream), "jx_gemm_swiglu_fwd");
   return launch<kSwigluF, false, false>(X, ldx, Wgu, K, p, reinterpret_cast<cudaStream_t>(stream),
                                         "jx_gemm_swiglu_fwd");
 }

@@ -15,6 +15,7 @@ Shapes (the operator workload of the Jishui-200M step):
   gemm     the decoder's GEMM shapes with their fused epilogues
   attn     causal flash attention fwd / bwd at (B 16, T 1024) and (B 4, T 4096), 16 heads x 64
   eval     validation forward (no autograd, fused head + CE) of the 200M model at 16 x 1024
+  decode   next-token logits with the KV cache vs re-running the whole context (200M, context ~1000)
 Each line is JSON with the time per call (CUDA events, after warm-up, inputs
 larger than L2 unless noted) and the achieved rate against the measured peaks.
 """
@@ -232,14 +233,50 @@ def bench_eval(iters: int) -> None:
           pk.get("bf16_tflops", 1590.0))
 
 
+def bench_decode(iters: int) -> None:
+    """Next-token logits at context 1024 of the 200M model: one KV-cache step against re-running the whole
+    context (what generate_torch.next_token_logits does, here through this library's forward)."""
+    from .config import jishui_200m
+    from .decode import KVCacheDecoder
+    from .model import JishuiForCausalLM
+    cfg = jishui_200m(1024)
+    torch.manual_seed(0)
+    model = JishuiForCausalLM(cfg).cuda()
+    with torch.no_grad():
+        for p in model.parameters():
+            if p.dim() == 2:
+                p.normal_(0.0, 0.02)
+    ctx = torch.randint(3, cfg.vocab_size, (1024,)).tolist()
+    dec = KVCacheDecoder(model)
+    dec.next_token_logits(ctx[:1000])
+    state = {"n": 1000}
+
+    def step():
+        if state["n"] >= 1024:
+            dec.next_token_logits(ctx[:1000])
+            state["n"] = 1000
+        state["n"] += 1
+        dec.next_token_logits(ctx[:state["n"]])
+
+    t = _time(step, iters)
+    print(json.dumps({"op": "decode step (KV cache) 200M, context ~1000", "us": t * 1e6,
+                      "tokens_per_s": 1.0 / t}), flush=True)
+    full = torch.tensor([ctx], device="cuda")
+    with torch.no_grad():
+        tf = _time(lambda: model(full)[0, -1].float().cpu(), max(2, iters // 4))
+    print(json.dumps({"op": "full-context recompute per token 200M, context 1024", "us": tf * 1e6,
+                      "tokens_per_s": 1.0 / tf}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--op", default="all", choices=("all", "rmsnorm", "ce", "adamw", "gemm", "attn", "eval"))
+    ap.add_argument("--op", default="all", choices=("all", "rmsnorm", "ce", "adamw", "gemm", "attn", "eval", "decode"))
     ap.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
     torch.cuda.set_device(0)
     for name, fn in (("rmsnorm", bench_rmsnorm), ("ce", bench_ce), ("adamw", bench_adamw), ("gemm", bench_gemm),
-                     ("attn", bench_attn), ("eval", bench_eval)):
+                     ("attn", bench_attn), ("eval", bench_eval),
+                     ("decode", bench_decode)):
         if a.op in ("all", name):
             fn(a.iters)
             torch.cuda.empty_cache()

@@ -151,6 +151,7 @@ class FlatParams:
                 view.copy_(p.detach().to(device=device, dtype=torch.float32))
                 p.data = view
         self._versions: list[int] | None = None
+        self.generation = 0  # bumped whenever the fp16 weights are rewritten (caches derived from them go stale)
         # Per-update state filled by GradScaler.unscale_ / clip_grad_norm_ and
         # consumed by the fused optimizer step.
         self.inv_scale: torch.Tensor | None = None
@@ -191,10 +192,12 @@ class FlatParams:
         if force or versions != self._versions:
             ops.cast_f32_f16(self.p32, self.p16)
             self._versions = versions
+            self.generation += 1
 
     def mark_f16_current(self) -> None:
         """Called after a fused update that rewrote p32 and p16 together."""
         self._versions = [p._version for p in self.params]
+        self.generation += 1
 
     def prepare_grads(self) -> bool:
         """Attaches flat-buffer views as `.grad`; returns True to accumulate into

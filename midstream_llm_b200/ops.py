@@ -303,6 +303,31 @@ def attn_bwd(qkv, o, do, lse, B, T, H, D, cos=None, sin=None, out=None, workspac
     return dqkv
 
 
+def attn_decode_workspace_bytes(B: int, H: int, max_len: int) -> int:
+    return _lib.query("jx_attn_decode_workspace_bytes", B, H, max_len)
+
+
+def attn_decode(qkv: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor, length: int, H: int, D: int,
+                workspace: torch.Tensor, out: torch.Tensor | None = None,
+                length_dev: torch.Tensor | None = None) -> torch.Tensor:
+    """One new token per sequence against the KV cache. qkv [B, 3*H*D] (the new rows), kcache / vcache
+    [B, max_len, H*D] holding positions < length-1; appends the new k / v at length-1; returns [B, H*D].
+    With `length_dev` (int32 scalar on the device) the length is read there and `length` is its upper bound."""
+    _check(qkv, F16, "qkv")
+    _check(kcache, F16, "kcache")
+    _check(vcache, F16, "vcache")
+    B = qkv.shape[0]
+    if kcache.stride() != vcache.stride() or kcache.shape[1] < length:
+        raise ValueError("attn_decode: caches must share a layout and hold `length` positions")
+    o = out if out is not None else torch.empty(B, H * D, device=qkv.device, dtype=F16)
+    if length_dev is not None and length_dev.dtype != torch.int32:
+        raise ValueError("attn_decode: length_dev must be int32")
+    _lib.call("jx_attn_decode", qkv.data_ptr(), _ld(qkv), kcache.data_ptr(), vcache.data_ptr(), kcache.stride(1),
+              kcache.stride(0), B, length, _ptr(length_dev), H, D, 1.0 / math.sqrt(D), workspace.data_ptr(),
+              o.data_ptr(), _ld(o), _stream())
+    return o
+
+
 # ---------------------------------------------------------------- cross-entropy
 def ce_fwd(logits16: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100, lse=None, row_loss=None):
     _check(targets, I64, "targets")

@@ -55,6 +55,34 @@ def test_gemm_resid(ops, gemm_mode):
     assert rel_err(c, ref) < TOL
 
 
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_small_m_products(ops, M):
+    """M <= 8 (incremental decoding) takes the weight-streaming path: plain, residual, q/k/v + RoPE at
+    arbitrary positions (a one-row slice of the tables) and SwiGLU, with the tiled kernels' rounding."""
+    N, K = 1056, 704
+    a, b, r = _h(M, K, seed=30), _h(N, K, seed=31), _h(M, N, seed=32)
+    assert rel_err(ops.gemm_f16(a, b), a.float() @ b.float().t()) < TOL
+    ref = r.float() + (a.float() @ b.float().t()).half().float()
+    assert rel_err(ops.gemm_f16(a, b, resid=r), ref) < TOL
+    H, hd, T = 3, 64, 512
+    d = H * hd
+    x, w = _h(M, d, seed=33), _h(3 * d, d, scale=0.05, seed=34)
+    cos, sin = _rope_tables(T, hd)
+    p0 = 300  # rows of the tables for positions p0 .. p0 + M - 1
+    out = ops.gemm_qkv_rope(x, w, d, cos[p0:p0 + M], sin[p0:p0 + M], M, hd)
+    lin = (x.float() @ w.float().t()).half().float()
+    q, k, v = lin.view(1, M, 3, H, hd).unbind(2)
+    cs, sn = cos[p0:p0 + M], sin[p0:p0 + M]
+    ref = torch.cat([_rope_ref(q, cs, sn).reshape(M, d), _rope_ref(k, cs, sn).reshape(M, d), v.reshape(M, d)], dim=1)
+    assert rel_err(out, ref) < TOL
+    F = 320
+    wgu = _h(2 * F, d, scale=0.05, seed=35)
+    gate, up, act = ops.gemm_swiglu_fwd(x, wgu, F)
+    assert rel_err(gate, x.float() @ wgu[:F].float().t()) < TOL
+    assert rel_err(up, x.float() @ wgu[F:].float().t()) < TOL
+    assert rel_err(act, torch.nn.functional.silu(gate.float()) * up.float()) < TOL
+
+
 def _rope_tables(T, hd, theta=10000.0):
     inv = theta ** (-torch.arange(0, hd, 2, device="cuda", dtype=torch.float32) / hd)
     ang = torch.arange(T, device="cuda", dtype=torch.float32)[:, None] * inv
