@@ -182,7 +182,28 @@ def run_reference(args) -> None:
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "mfu_model_flops": base["value"] * f_model}
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_RESULT_FD: int | None = None
+
+
+def _keep_stdout_for_result() -> None:
+    """The driver reads one JSON line from stdout: anything else that writes to file descriptor 1 (NCCL's
+    version banner, library warnings) is sent to stderr, and the result goes to the original stdout."""
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    out = json.dumps(line) + "\n"
+    if _RESULT_FD is None:
+        sys.stdout.write(out)
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, out.encode())
 
 
 def main() -> None:
@@ -195,6 +216,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
+    _keep_stdout_for_result()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
@@ -324,7 +346,7 @@ def main() -> None:
                            "h2d_bytes_per_step": B * (T + 1) * 8 * accum, "d2h_bytes_per_step": 3 * 4}
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+        emit(line)
     ctx.close()
 
 
