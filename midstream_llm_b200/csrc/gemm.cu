@@ -218,6 +218,15 @@ struct Stager {
       *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
+  // 32 values already packed as fp16 pairs (16 words).
+  __device__ __forceinline__ void put_packed(int part, const uint32_t (&w)[16]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = part * 4 + j;
+      *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+          make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    }
+  }
   __device__ __forceinline__ void flush(const CUtensorMap* map, int x, int y) {
     fence_proxy_async_smem();
     __syncwarp();
@@ -225,6 +234,25 @@ struct Stager {
       tma_store_2d(map, buf, x, y);
       bulk_commit();
     }
+  }
+};
+
+// Per-warp TMA staging of the epilogue's row-wise inputs (gate and up boxes of 32 rows x 64
+// columns, 128B-swizzled): one mbarrier, its phase, and the two tensor maps.
+constexpr uint32_t kAuxWarpBytes = 2 * 32 * 64 * 2;  // gate + up box of 32 rows x 64 fp16 columns
+
+struct AuxTma {
+  uint8_t* buf;
+  uint64_t* bar;
+  uint32_t phase;
+  const CUtensorMap* gate;
+  const CUtensorMap* up;
+  volatile int* abort_flag;
+  __device__ __forceinline__ void issue(int x, int y) {  // lane 0 only
+    fence_proxy_async_smem();  // earlier generic reads of the buffer happen before the refill
+    mbar_expect_tx(bar, kAuxWarpBytes);
+    tma_load_2d(buf, gate, bar, x, y);
+    tma_load_2d(buf + kAuxWarpBytes / 2, up, bar, x, y);
   }
 };
 
@@ -243,7 +271,7 @@ struct OutMaps {
 // weight-gradient output with direct 16-byte accesses.
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om, Stager& st, uint32_t tacc,
-                                              int quarter, int half, int lane, int mb, int nb, int split) {
+                                              int quarter, int half, int lane, int mb, int nb, int split, AuxTma* aux = nullptr) {
   const int row = mb * BM + quarter * 32 + lane;
   const int yrow = mb * BM + quarter * 32;  // first row of this warp's TMA boxes
   const uint32_t tl = tacc + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -408,22 +436,45 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
       const int c0 = half * 4 + cp * 2;
       const int col0 = nb * BN + c0 * 32;
       if (col0 >= F) break;
-      uint32_t r0[32], r1[32];
-      tmem_ld32(tl + c0 * 32, r0);
-      tmem_ld32(tl + c0 * 32 + 32, r1);
-      uint4 g0[4], g1[4], u0[4], u1[4];
-      load_raw32(p.aux0, p.ld_aux, row, col0, p.M, F, g0);
-      load_raw32(p.aux0, p.ld_aux, row, col0 + 32, p.M, F, g1);
-      load_raw32(p.aux1, p.ld_aux, row, col0, p.M, F, u0);
-      load_raw32(p.aux1, p.ld_aux, row, col0 + 32, p.M, F, u1);
-      tmem_ld_wait();
-      float dg[2][32], du[2][32];
+      // One 32-column part at a time (TMEM and the gate / up rows in, fp16 pairs out), so the
+      // live state stays small enough for the loads of a part to be in flight together.
+      uint4 ga[8], ua[8];  // this row's 64 gate / up values, from the TMA boxes when staged
+      if (aux) {
+        // The caller requested this tile's first box; this warp requests the second as soon as
+        // the first is in registers, so its load overlaps the arithmetic below.
+        if (!warp_wait_bar(aux->bar, aux->phase, aux->abort_flag, p.status, kStatusGemmEpilogueWait)) return;
+        aux->phase ^= 1u;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int off = lane * 128 + ((c ^ (lane & 7)) << 4);
+          ga[c] = *reinterpret_cast<const uint4*>(aux->buf + off);
+          ua[c] = *reinterpret_cast<const uint4*>(aux->buf + kAuxWarpBytes / 2 + off);
+        }
+        __syncwarp();
+        const int next_col = nb * BN + (half * 4 + 2) * 32;
+        if (cp == 0 && next_col < F && lane == 0) aux->issue(next_col, yrow);
+      }
+      uint32_t pdg[2][16], pdu[2][16];
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
+        uint32_t r[32];
+        tmem_ld32(tl + c0 * 32 + part * 32, r);
+        uint4 gq[4], uq[4];
+        if (aux) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            gq[j] = ga[part * 4 + j];
+            uq[j] = ua[part * 4 + j];
+          }
+        } else {
+          load_raw32(p.aux0, p.ld_aux, row, col0 + part * 32, p.M, F, gq);
+          load_raw32(p.aux1, p.ld_aux, row, col0 + part * 32, p.M, F, uq);
+        }
+        tmem_ld_wait();
         float d[32], g[32], u[32];
-        to_f32(part ? r1 : r0, d);
-        unpack32(part ? g1 : g0, g);
-        unpack32(part ? u1 : u0, u);
+        to_f32(r, d);
+        unpack32(gq, g);
+        unpack32(uq, u);
         float sig[32], s16[32], ds[32];
         round_all(d);
 #pragma unroll
@@ -435,18 +486,22 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
         round_all(s16);
         round_all(ds);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          du[part][i] = __fmul_rn(d[i], s16[i]);
-          dg[part][i] = __fmul_rn(__fmul_rn(ds[i], sig[i]), 1.0f + __fmul_rn(g[i], 1.0f - sig[i]));
+        for (int i = 0; i < 32; i += 2) {
+          const float du0 = __fmul_rn(d[i], s16[i]), du1 = __fmul_rn(d[i + 1], s16[i + 1]);
+          const float dg0 = __fmul_rn(__fmul_rn(ds[i], sig[i]), 1.0f + __fmul_rn(g[i], 1.0f - sig[i]));
+          const float dg1 = __fmul_rn(__fmul_rn(ds[i + 1], sig[i + 1]), 1.0f + __fmul_rn(g[i + 1], 1.0f - sig[i + 1]));
+          __half2 hg = __floats2half2_rn(dg0, dg1), hu = __floats2half2_rn(du0, du1);
+          pdg[part][i / 2] = *reinterpret_cast<uint32_t*>(&hg);
+          pdu[part][i / 2] = *reinterpret_cast<uint32_t*>(&hu);
         }
       }
       st.begin();
-      st.put32(0, dg[0]);
-      st.put32(1, dg[1]);
+      st.put_packed(0, pdg[0]);
+      st.put_packed(1, pdg[1]);
       st.flush(om.c0, col0, yrow);
       st.begin();
-      st.put32(0, du[0]);
-      st.put32(1, du[1]);
+      st.put_packed(0, pdu[0]);
+      st.put_packed(1, pdu[1]);
       st.flush(om.c1, col0, yrow);
     }
   }
@@ -625,7 +680,15 @@ constexpr int STAGES2 = 6;
 constexpr uint32_t kAHalf = 128 * BK * 2;  // 16 KiB
 constexpr uint32_t kBHalf = 128 * BK * 2;  // 16 KiB
 constexpr uint32_t kStage2Bytes = kAHalf + kBHalf;
-constexpr size_t kSmem2Bytes = 1024 + STAGES2 * kStage2Bytes + kEpiWarps * kStageOutBytes + 256;
+// The SwiGLU-backward epilogue reads gate / up boxes through TMA into per-warp shared memory
+// (kAuxWarpBytes per epilogue warp), paid for with a 4-stage ring.
+template <int EPI>
+__host__ __device__ constexpr int stages2() { return EPI == kSwigluB ? 4 : STAGES2; }
+template <int EPI>
+__host__ __device__ constexpr size_t smem2_bytes() {
+  return 1024 + stages2<EPI>() * kStage2Bytes + kEpiWarps * kStageOutBytes +
+         (EPI == kSwigluB ? kEpiWarps * kAuxWarpBytes : 0) + 320;
+}
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -687,18 +750,22 @@ template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC0, const __grid_constant__ CUtensorMap tmC1,
-                 const __grid_constant__ CUtensorMap tmC2, const Params p) {
+                 const __grid_constant__ CUtensorMap tmC2, const __grid_constant__ CUtensorMap tmX0,
+                 const __grid_constant__ CUtensorMap tmX1, const Params p) {
+  constexpr int S2 = stages2<EPI>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
-  uint8_t* smB = smem + STAGES2 * kAHalf;
-  uint8_t* sOut = smem + STAGES2 * kStage2Bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kEpiWarps * kStageOutBytes);
+  uint8_t* smB = smem + S2 * kAHalf;
+  uint8_t* sOut = smem + S2 * kStage2Bytes;
+  uint8_t* sAux = sOut + kEpiWarps * kStageOutBytes;  // kSwigluB only: [kEpiWarps][gate | up] boxes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sAux + (EPI == kSwigluB ? kEpiWarps * kAuxWarpBytes : 0));
   uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES2;
-  uint64_t* acc_full = bars + 2 * STAGES2;
-  uint64_t* acc_empty = bars + 2 * STAGES2 + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
+  uint64_t* empty = bars + S2;
+  uint64_t* acc_full = bars + 2 * S2;
+  uint64_t* acc_empty = bars + 2 * S2 + 2;
+  uint64_t* aux_full = bars + 2 * S2 + 4;  // one per epilogue warp (kSwigluB)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S2 + 4 + kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -707,7 +774,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool leader = (rank == 0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES2; ++s) {
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&aux_full[w], 1);
+    for (int s = 0; s < S2; ++s) {
       mbar_init(&full[s], 1);   // leader's producer arms it; both CTAs' TMA bytes complete it
       mbar_init(&empty[s], 1);  // the leader's MMA commit arrives in both CTAs
     }
@@ -749,8 +817,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb0 = s * p.kb_per_split;
         const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const uint32_t stage = it % STAGES2;
-          if (!wait_bar(&empty[stage], ((it / STAGES2) & 1u) ^ 1u, abort_flag, p.status, kStatusGemmProducerWait)) {
+          const uint32_t stage = it % S2;
+          if (!wait_bar(&empty[stage], ((it / S2) & 1u) ^ 1u, abort_flag, p.status, kStatusGemmProducerWait)) {
             ok = false;
             break;
           }
@@ -795,8 +863,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const uint32_t stage = it % STAGES2;
-          if (!wait_bar(&full[stage], (it / STAGES2) & 1u, abort_flag, p.status, kStatusGemmMmaWait)) {
+          const uint32_t stage = it % S2;
+          if (!wait_bar(&full[stage], (it / S2) & 1u, abort_flag, p.status, kStatusGemmMmaWait)) {
             ok = false;
             break;
           }
@@ -823,14 +891,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const OutMaps om{&tmC0, &tmC1, &tmC2};
     const uint32_t leader_acc_empty0 = map_to_rank(smem_u32(&acc_empty[0]), 0);
     const uint32_t leader_acc_empty1 = map_to_rank(smem_u32(&acc_empty[1]), 0);
+    AuxTma aux{sAux + (warp - 2) * kAuxWarpBytes, &aux_full[warp - 2], 0u, &tmX0, &tmX1, abort_flag};
     int local = 0;
     for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
       int mb2, nb, s;
       tile_coords2(p, t, mb2, nb, s);
       const int acc = local & 1;
+      if constexpr (EPI == kSwigluB) {
+        // This warp's first gate / up boxes of the tile load while the accumulator is awaited.
+        const int x = nb * BN + half * 4 * 32, y = (mb2 * 2 + (int)rank) * BM + quarter * 32;
+        if (x < p.swiglu_F && lane == 0) aux.issue(x, y);
+      }
       if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
-      epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb2 * 2 + (int)rank, nb, s);
+      epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb2 * 2 + (int)rank, nb, s,
+                         EPI == kSwigluB ? &aux : nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
@@ -1083,6 +1158,12 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
          make_tmap_f16(&tc1, p.C + p.swiglu_F, p.swiglu_F, p.M, p.ldc, 64, 32);
   }
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for the output", name);
+  // The SwiGLU-backward epilogue's gate / up inputs, read as 32 x 64 boxes.
+  CUtensorMap tx0 = tc0, tx1 = tc0;
+  if constexpr (EPI == kSwigluB)
+    ok = make_tmap_f16(&tx0, p.aux0, p.swiglu_F, p.M, p.ld_aux, 64, 32) &&
+         make_tmap_f16(&tx1, p.aux1, p.swiglu_F, p.M, p.ld_aux, 64, 32);
+  JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for an epilogue input", name);
 
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (EPI == kSwigluF) ? (p.swiglu_F + 127) / 128 : (p.N + BN - 1) / BN;
@@ -1102,13 +1183,13 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmem2Bytes;
+    cfg.dynamicSmemBytes = smem2_bytes<EPI>();
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (!max_clusters) {
       JX_CUDA_TRY(cudaFuncSetAttribute(gemm2_kernel<EPI, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmem2Bytes),
+                                       (int)smem2_bytes<EPI>()),
                   name);
       cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
       int n = 0;
@@ -1118,7 +1199,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
     const int tiles2 = ((p.tiles_m + 1) / 2) * p.tiles_n * p.splits;
     const int clusters = tiles2 < max_clusters ? tiles2 : max_clusters;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    JX_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm2_kernel<EPI, A_MN, B_MN>, ta, tb, tc0, tc1, tc2, p), name);
+    JX_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm2_kernel<EPI, A_MN, B_MN>, ta, tb, tc0, tc1, tc2, tx0, tx1, p), name);
     JX_CHECK_LAUNCH(name);
     return JX_OK;
   }
