@@ -66,6 +66,7 @@ struct Params {
   const float* rope_sin;
   int rope_seq;
   int rope_cols;
+  int rope_tma;  // kRope, 2-SM: cos / sin rows of a warp read as one TMA box each (rope_seq % 32 == 0)
   float* G;
   int64_t ldg;
   int accumulate;
@@ -348,6 +349,11 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
     }
   } else if constexpr (EPI == kRope) {
     const int pos = p.rope_seq > 0 ? row % p.rope_seq : 0;
+    // Staged: the caller requested this warp's cos / sin box (rows yrow % rope_seq .. +31, 128B-swizzled).
+    if (aux && nb * BN + half * 128 < p.rope_cols) {
+      if (!warp_wait_bar(aux->bar, aux->phase, aux->abort_flag, p.status, kStatusGemmEpilogueWait)) return;
+      aux->phase ^= 1u;
+    }
 #pragma unroll 1
     for (int hh = 0; hh < 2; ++hh) {
       const int h = half * 2 + hh;
@@ -365,7 +371,15 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
         const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + (int64_t)pos * 32);
 #pragma unroll
         for (int i4 = 0; i4 < 8; ++i4) {
-          const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+          float4 c4, s4;
+          if (aux) {
+            const int off = lane * 128 + ((i4 ^ (lane & 7)) << 4);
+            c4 = *reinterpret_cast<const float4*>(aux->buf + off);
+            s4 = *reinterpret_cast<const float4*>(aux->buf + kAuxWarpBytes / 2 + off);
+          } else {
+            c4 = __ldg(cs + i4);
+            s4 = __ldg(sn + i4);
+          }
           const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -382,6 +396,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
       st.put32(1, b);
       st.flush(om.c0, col, yrow);
     }
+    if (aux) __syncwarp();  // every lane's box reads done before the next tile's refill
   } else if constexpr (EPI == kSwigluF) {
     const int F = p.swiglu_F;
     const int col = nb * 128 + half * 64;  // 64 gate columns (and the matching up columns)
@@ -680,14 +695,17 @@ constexpr int STAGES2 = 6;
 constexpr uint32_t kAHalf = 128 * BK * 2;  // 16 KiB
 constexpr uint32_t kBHalf = 128 * BK * 2;  // 16 KiB
 constexpr uint32_t kStage2Bytes = kAHalf + kBHalf;
-// The SwiGLU-backward epilogue reads gate / up boxes through TMA into per-warp shared memory
-// (kAuxWarpBytes per epilogue warp), paid for with a 4-stage ring.
+// The SwiGLU-backward and RoPE epilogues read their row-wise inputs (gate / up boxes, cos / sin
+// rows) through TMA into per-warp shared memory (kAuxWarpBytes per epilogue warp), paid for with a
+// 4-stage ring.
 template <int EPI>
-__host__ __device__ constexpr int stages2() { return EPI == kSwigluB ? 4 : STAGES2; }
+__host__ __device__ constexpr bool has_aux2() { return EPI == kSwigluB || EPI == kRope; }
+template <int EPI>
+__host__ __device__ constexpr int stages2() { return has_aux2<EPI>() ? 4 : STAGES2; }
 template <int EPI>
 __host__ __device__ constexpr size_t smem2_bytes() {
   return 1024 + stages2<EPI>() * kStage2Bytes + kEpiWarps * kStageOutBytes +
-         (EPI == kSwigluB ? kEpiWarps * kAuxWarpBytes : 0) + 320;
+         (has_aux2<EPI>() ? kEpiWarps * kAuxWarpBytes : 0) + 320;
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -758,13 +776,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smA = smem;
   uint8_t* smB = smem + S2 * kAHalf;
   uint8_t* sOut = smem + S2 * kStage2Bytes;
-  uint8_t* sAux = sOut + kEpiWarps * kStageOutBytes;  // kSwigluB only: [kEpiWarps][gate | up] boxes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sAux + (EPI == kSwigluB ? kEpiWarps * kAuxWarpBytes : 0));
+  uint8_t* sAux = sOut + kEpiWarps * kStageOutBytes;  // kSwigluB / kRope: [kEpiWarps][gate | up] or [cos | sin]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sAux + (has_aux2<EPI>() ? kEpiWarps * kAuxWarpBytes : 0));
   uint64_t* full = bars;
   uint64_t* empty = bars + S2;
   uint64_t* acc_full = bars + 2 * S2;
   uint64_t* acc_empty = bars + 2 * S2 + 2;
-  uint64_t* aux_full = bars + 2 * S2 + 4;  // one per epilogue warp (kSwigluB)
+  uint64_t* aux_full = bars + 2 * S2 + 4;  // one per epilogue warp (kSwigluB, kRope)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S2 + 4 + kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -901,11 +919,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // This warp's first gate / up boxes of the tile load while the accumulator is awaited.
         const int x = nb * BN + half * 4 * 32, y = (mb2 * 2 + (int)rank) * BM + quarter * 32;
         if (x < p.swiglu_F && lane == 0) aux.issue(x, y);
+      } else if constexpr (EPI == kRope) {
+        // The cos / sin rows of this warp's 32 token rows (consecutive positions).
+        const int y = (mb2 * 2 + (int)rank) * BM + quarter * 32;
+        if (p.rope_tma && nb * BN + half * 128 < p.rope_cols && lane == 0) aux.issue(0, y % p.rope_seq);
       }
       if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
       epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb2 * 2 + (int)rank, nb, s,
-                         EPI == kSwigluB ? &aux : nullptr);
+                         (EPI == kSwigluB || (EPI == kRope && p.rope_tma)) ? &aux : nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
@@ -1163,6 +1185,14 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
   if constexpr (EPI == kSwigluB)
     ok = make_tmap_f16(&tx0, p.aux0, p.swiglu_F, p.M, p.ld_aux, 64, 32) &&
          make_tmap_f16(&tx1, p.aux1, p.swiglu_F, p.M, p.ld_aux, 64, 32);
+  // The RoPE epilogue's cos / sin tables ([rope_seq, 32] fp32): a warp's 32 rows are 32 consecutive
+  // positions when rope_seq is a multiple of 32, one 32 x 32 box per table.
+  if constexpr (EPI == kRope) {
+    p.rope_tma = two_sm && p.rope_seq % 32 == 0;
+    if (p.rope_tma)
+      ok = make_tmap_f32(&tx0, p.rope_cos, 32, p.rope_seq, 32, 32, 32) &&
+           make_tmap_f32(&tx1, p.rope_sin, 32, p.rope_seq, 32, 32, 32);
+  }
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for an epilogue input", name);
 
   p.tiles_m = (p.M + BM - 1) / BM;
@@ -1258,6 +1288,7 @@ extern "C" int jx_gemm_qkv_rope(const void* X, int64_t ldx, const void* W, int M
   JX_CHECK_ARG(head_dim == 64, "jx_gemm_qkv_rope: head_dim must be 64 (got %d)", head_dim);
   JX_CHECK_ARG(hidden % 64 == 0, "jx_gemm_qkv_rope: hidden must be a multiple of 64");
   JX_CHECK_ARG(rope_cos && rope_sin && seq_len > 0, "jx_gemm_qkv_rope: missing RoPE tables");
+  JX_CHECK_ARG(aligned16(rope_cos) && aligned16(rope_sin), "jx_gemm_qkv_rope: RoPE tables must be 16-byte aligned");
   JX_CHECK_ARG(C && aligned16(C) && ldc % 8 == 0, "jx_gemm_qkv_rope: bad output");
   Params p = base_params(M, 3 * hidden, K);
   p.C = static_cast<__half*>(C);

@@ -110,6 +110,40 @@ def test_gemm_qkv_rope(ops, gemm_mode):
     assert rel_err(out, ref) < TOL
 
 
+@pytest.mark.parametrize("B,T,H", [(3, 256, 5), (5, 96, 4), (3, 200, 4)])
+def test_gemm_qkv_rope_shapes(ops, gemm_mode, B, T, H):
+    """The 2-SM RoPE epilogue reads a warp's 32 cos / sin rows as TMA boxes when seq_len % 32 == 0 and
+    row by row otherwise. Shapes: a tile whose columns straddle the end of q|k (H=5), a partial last
+    row tile, seq_len 200."""
+    hd = 64
+    d = H * hd
+    x = _h(B * T, d, seed=40)
+    w = _h(3 * d, d, scale=0.05, seed=41)
+    cos, sin = _rope_tables(T, hd)
+    out = ops.gemm_qkv_rope(x, w, d, cos, sin, T, hd)
+    lin = (x.float() @ w.float().t()).half().float()
+    q, k, v = lin.view(B, T, 3, H, hd).unbind(2)
+    ref = torch.cat([_rope_ref(q, cos, sin).reshape(B * T, d), _rope_ref(k, cos, sin).reshape(B * T, d),
+                     v.reshape(B * T, d)], dim=1)
+    assert rel_err(out, ref) < TOL
+
+
+def test_gemm_qkv_rope_table_paths(ops, gemm_mode):
+    """One sequence of 768 rows with tables of 769 rows: seq_len 768 (boxes on the 2-SM path) and 769
+    (row-by-row reads) rotate every row by the same position, so the outputs are bit-identical.
+    Tables that are not 16-byte aligned are rejected on the host."""
+    T, H, hd = 768, 5, 64
+    d = H * hd
+    x = _h(T, d, seed=42)
+    w = _h(3 * d, d, scale=0.05, seed=43)
+    cos, sin = _rope_tables(T + 1, hd)
+    assert torch.equal(ops.gemm_qkv_rope(x, w, d, cos, sin, T, hd), ops.gemm_qkv_rope(x, w, d, cos, sin, T + 1, hd))
+    from midstream_llm_b200._lib import JxError
+    buf = torch.zeros(cos.numel() + 1, device="cuda", dtype=torch.float32)
+    with pytest.raises(JxError, match="16-byte aligned"):
+        ops.gemm_qkv_rope(x, w, d, buf[1:].view(T + 1, hd // 2), sin, T + 1, hd)
+
+
 def test_swiglu_fwd_bwd(ops, gemm_mode):
     M, d, F = 512, 256, 688
     x = _h(M, d, seed=6)
