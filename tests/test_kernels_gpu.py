@@ -55,6 +55,18 @@ def test_gemm_resid(ops, gemm_mode):
     assert rel_err(c, ref) < TOL
 
 
+@pytest.mark.parametrize("M,N,K", [(600, 1056, 704), (1000, 200, 256)])
+def test_gemm_resid_ragged(ops, gemm_mode, M, N, K):
+    """Residual add with row tiles past M, a last column chunk past N, a residual with its own row
+    stride, and in place (the output overwriting the residual)."""
+    a, b = _h(M, K, seed=12), _h(N, K, seed=13)
+    r = _h(M, N + 40, seed=14)[:, :N]  # leading dimension N + 40
+    ref = r.float() + (a.float() @ b.float().t()).half().float()
+    assert rel_err(ops.gemm_f16(a, b, resid=r), ref) < TOL
+    r2 = r.contiguous()
+    assert rel_err(ops.gemm_f16(a, b, resid=r2, out=r2), ref) < TOL
+
+
 @pytest.mark.parametrize("M", [1, 3, 8])
 def test_small_m_products(ops, M):
     """M <= 8 (incremental decoding) takes the weight-streaming path: plain, residual, q/k/v + RoPE at
