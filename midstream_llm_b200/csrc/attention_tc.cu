@@ -26,6 +26,7 @@
 // q/k/v are read in place from the fused projection output [B*T, 3*H*64] by
 // one TMA descriptor; O is written token-major [B*T, H*64].
 #include <algorithm>
+#include <type_traits>
 
 #include "jx_common.cuh"
 #include "jx_host.h"
@@ -496,7 +497,7 @@ __device__ __forceinline__ void rope_back(float& g1, float& g2, const float* cs,
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_dq,
-                       const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq_acc,
+                       const float* __restrict__ neg_lse_log2, const float* __restrict__ delta, float* __restrict__ dq_acc,
                        __half* __restrict__ dqkv, int T, int H, float scale, float scale_log2,
                        const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, int* status) {
   extern __shared__ uint8_t smem_raw[];
@@ -519,7 +520,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int d = H * D;
   const int row_base = b * T;
   const int ntiles = nqb - kb;  // query tiles kb .. nqb-1
-  const float log2e = 1.4426950408889634f;
   (void)dq_acc;
 
   if (threadIdx.x == 0) {
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  const float* lse_bh = lse + ((int64_t)b * H + h) * T;
+  const float* lse_bh = neg_lse_log2 + ((int64_t)b * H + h) * T;  // -LSE * log2(e) per query
   const float* delta_bh = delta + ((int64_t)b * H + h) * T;
 
   if (warp == 0) {
@@ -687,46 +687,54 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const float* Ls = sL + s * BQ;
       const float* Ds = sD + s * BQ;
       const int lim = diag ? key - qi * BQ : -1;  // on the diagonal tile, queries at index < lim are masked
-#pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        // 32 queries: S^T / dP^T in, P^T / dS^T (fp16 pairs) back over the first 16 columns of
-        // this warp's half (already read), dS^T also to shared memory.
-        const int q0 = colh * 64 + ch * 32;
-        uint32_t sr[32], dr[32];
-        tmem_ld32(lane_base + q0, sr);
-        tmem_ld32(lane_base + 128 + q0, dr);
-        tmem_ld_wait();
-        uint32_t pw[16], sw[16];
-#pragma unroll
-        for (int gq = 0; gq < 8; ++gq) {  // 4 queries per group: LSE / Delta as float4 (broadcast reads)
-          const float4 L4 = *reinterpret_cast<const float4*>(Ls + q0 + gq * 4);
-          const float4 D4 = *reinterpret_cast<const float4*>(Ds + q0 + gq * 4);
-          const float nl[4] = {-L4.x * log2e, -L4.y * log2e, -L4.z * log2e, -L4.w * log2e};
-          const float dl[4] = {D4.x, D4.y, D4.z, D4.w};
-          float pv[4], dv[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int qc = gq * 4 + u;
-            float p = ex2(fmaf(__uint_as_float(sr[qc]), scale_log2, nl[u]));
-            if (diag && q0 + qc < lim) p = 0.f;
-            pv[u] = p;
-            dv[u] = p * (__uint_as_float(dr[qc]) - dl[u]);
+      // The diagonal tile masks queries before this thread's key; the other tiles compile without the test.
+      auto softmax_tile = [&](auto diag_tag) {
+        constexpr bool kDiag = decltype(diag_tag)::value;
+  #pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          // 32 queries: S^T / dP^T in, P^T / dS^T (fp16 pairs) back over the first 16 columns of
+          // this warp's half (already read), dS^T also to shared memory.
+          const int q0 = colh * 64 + ch * 32;
+          uint32_t sr[32], dr[32];
+          tmem_ld32(lane_base + q0, sr);
+          tmem_ld32(lane_base + 128 + q0, dr);
+          tmem_ld_wait();
+          uint32_t pw[16], sw[16];
+  #pragma unroll
+          for (int gq = 0; gq < 8; ++gq) {  // 4 queries per group: LSE / Delta as float4 (broadcast reads)
+            const float4 L4 = *reinterpret_cast<const float4*>(Ls + q0 + gq * 4);
+            const float4 D4 = *reinterpret_cast<const float4*>(Ds + q0 + gq * 4);
+            const float nl[4] = {L4.x, L4.y, L4.z, L4.w};
+            const float dl[4] = {D4.x, D4.y, D4.z, D4.w};
+            float pv[4], dv[4];
+  #pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int qc = gq * 4 + u;
+              float p = ex2(fmaf(__uint_as_float(sr[qc]), scale_log2, nl[u]));
+              if (kDiag && q0 + qc < lim) p = 0.f;
+              pv[u] = p;
+              dv[u] = p * (__uint_as_float(dr[qc]) - dl[u]);
+            }
+            __half2 hp0 = __floats2half2_rn(pv[0], pv[1]), hp1 = __floats2half2_rn(pv[2], pv[3]);
+            __half2 hs0 = __floats2half2_rn(dv[0], dv[1]), hs1 = __floats2half2_rn(dv[2], dv[3]);
+            pw[gq * 2] = *reinterpret_cast<uint32_t*>(&hp0);
+            pw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hp1);
+            sw[gq * 2] = *reinterpret_cast<uint32_t*>(&hs0);
+            sw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hs1);
           }
-          __half2 hp0 = __floats2half2_rn(pv[0], pv[1]), hp1 = __floats2half2_rn(pv[2], pv[3]);
-          __half2 hs0 = __floats2half2_rn(dv[0], dv[1]), hs1 = __floats2half2_rn(dv[2], dv[3]);
-          pw[gq * 2] = *reinterpret_cast<uint32_t*>(&hp0);
-          pw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hp1);
-          sw[gq * 2] = *reinterpret_cast<uint32_t*>(&hs0);
-          sw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hs1);
+          tmem_st16(lane_base + colh * 64 + ch * 16, pw);
+          tmem_st16(lane_base + 128 + colh * 64 + ch * 16, sw);
+  #pragma unroll
+          for (int c = 0; c < 4; ++c) {  // 4 chunks of 8 queries
+            const int off = ((ch * 4 + c) ^ (r & 7)) << 4;
+            *reinterpret_cast<uint4*>(srow + off) = make_uint4(sw[c * 4], sw[c * 4 + 1], sw[c * 4 + 2], sw[c * 4 + 3]);
+          }
         }
-        tmem_st16(lane_base + colh * 64 + ch * 16, pw);
-        tmem_st16(lane_base + 128 + colh * 64 + ch * 16, sw);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {  // 4 chunks of 8 queries
-          const int off = ((ch * 4 + c) ^ (r & 7)) << 4;
-          *reinterpret_cast<uint4*>(srow + off) = make_uint4(sw[c * 4], sw[c * 4 + 1], sw[c * 4 + 2], sw[c * 4 + 3]);
-        }
-      }
+      };
+      if (diag)
+        softmax_tile(std::true_type{});
+      else
+        softmax_tile(std::false_type{});
       tmem_st_wait();
       tc_fence_before();
       fence_proxy_async_smem();
@@ -859,13 +867,14 @@ extern "C" int jx_attn_fwd(const void* qkv, void* out, float* lse, void* workspa
 }
 
 extern "C" int64_t jx_attn_bwd_workspace_bytes(int B, int T, int H, int Dh) {
-  return (int64_t)B * H * T * 4 + (int64_t)B * T * H * Dh * 4;
+  return 2 * (int64_t)B * H * T * 4 + (int64_t)B * T * H * Dh * 4;  // Delta, -LSE log2(e), dQ accumulator
 }
 
 // Delta = rowsum(dO * O), computed by attn_delta_kernel in attention.cu.
 namespace jx {
 namespace attn {
-void launch_delta(const __half* out, const __half* dout, float* delta, int B, int T, int H, cudaStream_t s);
+void launch_delta(const __half* out, const __half* dout, const float* lse, float* delta, float* neg_lse_log2, int B,
+                  int T, int H, cudaStream_t s);
 }
 }  // namespace jx
 
@@ -881,17 +890,18 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
   JX_CHECK_ARG((rope_cos == nullptr) == (rope_sin == nullptr), "jx_attn_bwd: pass both RoPE tables or neither");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   float* delta = static_cast<float*>(workspace);
-  float* dq_acc = delta + (int64_t)B * H * T;
+  float* nl2 = delta + (int64_t)B * H * T;
+  float* dq_acc = nl2 + (int64_t)B * H * T;
   const int64_t rows = (int64_t)B * T;
   const int d = H * D;
   CUtensorMap tq, tdo;
   JX_CHECK_ARG(make_tmap_f16(&tq, qkv, 3LL * d, rows, 3LL * d, D, BKV), "jx_attn_bwd: cannot encode TMA descriptor");
   JX_CHECK_ARG(make_tmap_f16(&tdo, dout, d, rows, d, D, BQ), "jx_attn_bwd: cannot encode TMA descriptor");
   CUtensorMap tdq;
-  JX_CHECK_ARG(make_tmap_f32(&tdq, static_cast<float*>(workspace) + (int64_t)B * H * T, d, rows, d, 32, 32),
+  JX_CHECK_ARG(make_tmap_f32(&tdq, dq_acc, d, rows, d, 32, 32),
                "jx_attn_bwd: cannot encode TMA descriptor for the dQ accumulator");
   JX_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)rows * d * sizeof(float), s), "jx_attn_bwd: clear dq accumulator");
-  jx::attn::launch_delta(static_cast<const __half*>(out), static_cast<const __half*>(dout), delta, B, T, H, s);
+  jx::attn::launch_delta(static_cast<const __half*>(out), static_cast<const __half*>(dout), lse, delta, nl2, B, T, H, s);
   JX_CHECK_LAUNCH("jx_attn_bwd: delta");
   static bool attr_set = false;
   if (!attr_set) {
@@ -900,7 +910,7 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
     attr_set = true;
   }
   dim3 grid(T / BKV, H, B);
-  attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, tdq, lse, delta, dq_acc, static_cast<__half*>(dqkv), T, H,
+  attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, tdq, nl2, delta, dq_acc, static_cast<__half*>(dqkv), T, H,
                                                         scale, scale * 1.4426950408889634f, rope_cos, rope_sin,
                                                         status_ptr());
   JX_CHECK_LAUNCH("jx_attn_bwd");
