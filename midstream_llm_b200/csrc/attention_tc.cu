@@ -436,10 +436,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Backward on tcgen05. One CTA per (128-key block, head, batch); the key
-// block's K and V stay in shared memory, dK and dV accumulate in TMEM across
-// the query tiles i = kb .. T/128-1. Each query tile (Q_i, dO_i, LSE_i,
-// Delta_i double-buffered by TMA) is processed as two halves of 64 queries,
+// Backward on tcgen05: a persistent kernel, one CTA per SM. A work item is one
+// 128-key block kb of one (head, batch); the CTAs take items from a global
+// counter, heaviest first (key block kb meets T/128 - kb query tiles) within
+// chunks of kBwdChunk (head, batch) pairs, so the last items anywhere are the
+// one-tile blocks. The key block's K and V stay in shared memory (two buffers,
+// one per item parity, so the next item's K / V load during this one's last
+// tiles); dK and dV accumulate in TMEM across the query tiles i = kb .. T/128-1.
+// Each query tile (Q_i, dO_i, -LSE_i log2(e), Delta_i: a two-slot ring filled
+// by TMA, running on across items) is processed as two halves of 64 queries,
 // pipelined against each other:
 //   S^T_h  = K Q_h^T   (M 128 keys, N 64 queries, K 64)    TMEM [64h, 64h+64)
 //   dP^T_h = V dO_h^T  (M 128, N 64, K 64)                 TMEM [128+64h, ...)
@@ -448,28 +453,46 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 //                  read, and dS^T also to 128B-swizzled shared memory (two buffers)
 //   dV += P^T_h dO_h   (M 128, N 64, K 64; P^T from TMEM, dO read MN-major)   TMEM [256,320)
 //   dK += dS^T_h Q_h   (M 128, N 64, K 64; dS^T from TMEM, Q read MN-major)   TMEM [320,384)
-//   then S^T_h / dP^T_h of tile i+1 (the tensor core runs one thread's products
-//   in issue order, so they follow the dV / dK reads of those columns); while
-//   the softmax of one half runs, the tensor core works on the other half.
+//   then S^T_h / dP^T_h of the next tile (of this item, or of the next item
+//   during this item's last tile): the tensor core runs one thread's products
+//   in issue order, so they follow the dV / dK reads of those columns.
 //   dQ_i = dS K        (M 128 queries, N 64, K 128 keys; dS^T in shared memory
 //                       read MN-major as the A operand, K read MN-major)     TMEM [384,512), two buffers
 //   dQ_i is added to an fp32 accumulator in global memory by TMA reduce-add
-//   while the products of tile i+1 run.
+//   (each warp stages its 32 x 32 block as two 64B-swizzled 32 x 16 halves)
+//   while the products of the next tile run.
+// At the end of an item the softmax warps drain dK / dV from TMEM (then the
+// next item's first dV / dK products may overwrite them) and store them while
+// the next item's first scores are computed.
 // Warps: 0 TMA producer, 1 MMA issuer, 2..9 softmax / epilogue (two warps per
 // TMEM lane quarter, each on half of the query columns).
 // ---------------------------------------------------------------------------
 constexpr int kBwdThreads = 320;
-constexpr uint32_t kDqStageBytes = 32 * 32 * 4;  // one warp's [32 rows x 32 cols] fp32 dQ block
-constexpr size_t kBwdSmem = 1024 + 2 * kTileBytes /*K,V*/ + 4 * kTileBytes /*Q,dO x2*/ + 2 * kPBytes /*dS^T x2*/ +
-                            8 * kDqStageBytes /*dQ staging*/ + 2 * 2 * BQ * sizeof(float) /*LSE, Delta x2*/ + 512;
+constexpr int kBwdChunk = 32;  // (head, batch) pairs per chunk of the backward's work order
+constexpr uint32_t kDqStageBytes = 32 * 16 * 4;  // one warp's [32 rows x 16 cols] fp32 half of its dQ block
+constexpr size_t kBwdSmem = 1024 + 4 * kTileBytes /*K,V x2*/ + 4 * kTileBytes /*Q,dO x2*/ + 2 * kPBytes /*dS^T x2*/ +
+                            8 * kDqStageBytes /*dQ staging*/ + 2 * 2 * BQ * sizeof(float) /*-LSE log2e, Delta x2*/ +
+                            512;
 
 struct BwdBars {
-  uint64_t kv_full;
-  uint64_t q_full[2], q_empty[2];
-  uint64_t sdp_full[2], p_full[2], grads_done, dq_free[2];  // sdp / p per query half
+  uint64_t kv_full[2], kv_empty[2];  // per K / V buffer (item parity)
+  uint64_t q_full[2], q_empty[2];    // per query-tile ring slot
+  uint64_t sdp_full[2], p_full[2];   // per query half
+  uint64_t grads_done, dq_free[2], acc_drained;
+  ItemRing items;
   uint32_t tmem_base;
   int abort;
 };
+
+struct BwdItem {
+  int kb, h, b;
+};
+
+__device__ __forceinline__ BwdItem bwd_decode(int idx, int nqb, int H, int B) {
+  int pair;
+  const int kb = chunked_rank(idx, nqb, kBwdChunk, H * B, &pair);
+  return BwdItem{kb, pair % H, pair / H};
+}
 
 // TMEM column (relative to the S^T or dP^T base) of the fp16 pair holding queries
 // 2c, 2c+1 of K step kk (16 queries): the softmax warp of column half h writes the
@@ -496,45 +519,40 @@ __device__ __forceinline__ void rope_back(float& g1, float& g2, const float* cs,
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                       const __grid_constant__ CUtensorMap tm_dq,
-                       const float* __restrict__ neg_lse_log2, const float* __restrict__ delta, float* __restrict__ dq_acc,
-                       __half* __restrict__ dqkv, int T, int H, float scale, float scale_log2,
-                       const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, int* status) {
+                       const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ neg_lse_log2, const float* __restrict__ delta,
+                       float* __restrict__ dq_acc, __half* __restrict__ dqkv, int* __restrict__ work_counter, int B,
+                       int T, int H, float scale, float scale_log2, const float* __restrict__ rope_cos,
+                       const float* __restrict__ rope_sin, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = smem;
-  uint8_t* sV = sK + kTileBytes;
-  uint8_t* sQ = sV + kTileBytes;             // 2 stages
-  uint8_t* sO = sQ + 2 * kTileBytes;         // dO, 2 stages
+  uint8_t* sKV = smem;                       // [2 buffers][K | V]
+  uint8_t* sQ = sKV + 4 * kTileBytes;        // query-tile ring, 2 slots
+  uint8_t* sO = sQ + 2 * kTileBytes;         // dO, 2 slots
   uint8_t* sSt = sO + 2 * kTileBytes;        // dS^T [128 keys x 128 queries], 2 buffers (tile parity)
-  uint8_t* sDq = sSt + 2 * kPBytes;          // [8 warps][32 x 32] fp32 dQ staging (128B-swizzled)
-  float* sL = reinterpret_cast<float*>(sDq + 8 * kDqStageBytes);  // [2][128]
-  float* sD = sL + 2 * BQ;                               // [2][128]
+  uint8_t* sDq = sSt + 2 * kPBytes;          // [8 warps][32 x 16] fp32 dQ staging (64B-swizzled)
+  float* sL = reinterpret_cast<float*>(sDq + 8 * kDqStageBytes);  // [2][128] -LSE log2(e)
+  float* sD = sL + 2 * BQ;                                   // [2][128] Delta
   BwdBars* bars = reinterpret_cast<BwdBars*>(sD + 2 * BQ);
   volatile int* abort_flag = &bars->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = T / BQ;
-  const int kb = blockIdx.x;  // key block; kb = 0 has the most query tiles and starts first
-  const int h = blockIdx.y, b = blockIdx.z;
   const int d = H * D;
-  const int row_base = b * T;
-  const int ntiles = nqb - kb;  // query tiles kb .. nqb-1
-  (void)dq_acc;
+  const int total = nqb * H * B;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->kv_full, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->kv_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
       mbar_init(&bars->q_full[s], 1);
       mbar_init(&bars->q_empty[s], 1);
-    }
-    for (int hf = 0; hf < 2; ++hf) {
-      mbar_init(&bars->sdp_full[hf], 1);
-      mbar_init(&bars->p_full[hf], 4);
+      mbar_init(&bars->sdp_full[s], 1);
+      mbar_init(&bars->p_full[s], 4);
+      mbar_init(&bars->dq_free[s], 8);
     }
     mbar_init(&bars->grads_done, 1);
-    mbar_init(&bars->dq_free[0], 8);
-    mbar_init(&bars->dq_free[1], 8);
+    mbar_init(&bars->acc_drained, 8);
+    ring_init(&bars->items);
     bars->abort = 0;
     fence_barrier_init();
   }
@@ -547,24 +565,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  const float* lse_bh = neg_lse_log2 + ((int64_t)b * H + h) * T;  // -LSE * log2(e) per query
-  const float* delta_bh = delta + ((int64_t)b * H + h) * T;
-
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_qkv);
       tma_prefetch_desc(&tm_do);
-      mbar_expect_tx(&bars->kv_full, 2 * kTileBytes);
-      tma_load_2d(sK, &tm_qkv, &bars->kv_full, d + h * D, row_base + kb * BKV);
-      tma_load_2d(sV, &tm_qkv, &bars->kv_full, 2 * d + h * D, row_base + kb * BKV);
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t & 1, qi = kb + t;
-        if (!wait(&bars->q_empty[s], ((t >> 1) & 1) ^ 1, abort_flag, status, kFaProducer)) break;
-        mbar_expect_tx(&bars->q_full[s], 2 * kTileBytes + 2 * BQ * sizeof(float));
-        tma_load_2d(sQ + s * kTileBytes, &tm_qkv, &bars->q_full[s], h * D, row_base + qi * BQ);
-        tma_load_2d(sO + s * kTileBytes, &tm_do, &bars->q_full[s], h * D, row_base + qi * BQ);
-        bulk_load(sL + s * BQ, lse_bh + qi * BQ, BQ * sizeof(float), &bars->q_full[s]);
-        bulk_load(sD + s * BQ, delta_bh + qi * BQ, BQ * sizeof(float), &bars->q_full[s]);
+      uint32_t g = 0;  // query tiles loaded so far (the ring runs on across items)
+      for (uint32_t n = 0;; ++n) {
+        const int idx = atomicAdd(work_counter, 1);
+        if (!ring_publish(&bars->items, n, idx, abort_flag, status, kFaProducer) || idx >= total) break;
+        const BwdItem it = bwd_decode(idx, nqb, H, B);
+        const int row_base = it.b * T;
+        const int kvb = n & 1;
+        if (!wait(&bars->kv_empty[kvb], ((n >> 1) & 1) ^ 1, abort_flag, status, kFaProducer)) break;
+        uint8_t* kv = sKV + kvb * 2 * kTileBytes;
+        mbar_expect_tx(&bars->kv_full[kvb], 2 * kTileBytes);
+        tma_load_2d(kv, &tm_qkv, &bars->kv_full[kvb], d + it.h * D, row_base + it.kb * BKV);
+        tma_load_2d(kv + kTileBytes, &tm_qkv, &bars->kv_full[kvb], 2 * d + it.h * D, row_base + it.kb * BKV);
+        const float* lse_bh = neg_lse_log2 + ((int64_t)it.b * H + it.h) * T;
+        const float* delta_bh = delta + ((int64_t)it.b * H + it.h) * T;
+        bool ok = true;
+        for (int qi = it.kb; qi < nqb; ++qi, ++g) {
+          const int s = g & 1;
+          if (!wait(&bars->q_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, status, kFaProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bars->q_full[s], 2 * kTileBytes + 2 * BQ * sizeof(float));
+          tma_load_2d(sQ + s * kTileBytes, &tm_qkv, &bars->q_full[s], it.h * D, row_base + qi * BQ);
+          tma_load_2d(sO + s * kTileBytes, &tm_do, &bars->q_full[s], it.h * D, row_base + qi * BQ);
+          bulk_load(sL + s * BQ, lse_bh + qi * BQ, BQ * sizeof(float), &bars->q_full[s]);
+          bulk_load(sD + s * BQ, delta_bh + qi * BQ, BQ * sizeof(float), &bars->q_full[s]);
+        }
+        if (!ok) break;
       }
     }
   } else if (warp == 1) {
@@ -574,188 +606,242 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t id_q = idesc_f16_f32(BQ, D, true, true);
       // Shared-memory descriptors are built once and advanced by constant additions: one
       // thread issues every product, and an N = 64 product is shorter than building two
-      // descriptors from addresses.
-      const uint64_t dK = smem_desc_sw128(smem_u32(sK), 16, 1024);      // K-major A of S^T
-      const uint64_t dV = smem_desc_sw128(smem_u32(sV), 16, 1024);      // K-major A of dP^T
-      const uint64_t dKmn = smem_desc_sw128(smem_u32(sK), 8192, 1024);  // MN-major B of dQ
-      const uint64_t dQk = smem_desc_sw128(smem_u32(sQ), 16, 1024);     // K-major B of S^T (stage 0)
+      // descriptors from addresses. K / V descriptors are for buffer 0 (+ 2 tiles for buffer 1).
+      const uint64_t dK = smem_desc_sw128(smem_u32(sKV), 16, 1024);               // K-major A of S^T
+      const uint64_t dV = smem_desc_sw128(smem_u32(sKV + kTileBytes), 16, 1024);  // K-major A of dP^T
+      const uint64_t dKmn = smem_desc_sw128(smem_u32(sKV), 8192, 1024);           // MN-major B of dQ
+      const uint64_t dQk = smem_desc_sw128(smem_u32(sQ), 16, 1024);               // K-major B of S^T (slot 0)
       const uint64_t dOk = smem_desc_sw128(smem_u32(sO), 16, 1024);
       const uint64_t dQmn = smem_desc_sw128(smem_u32(sQ), 8192, 1024);  // MN-major B of dK
       const uint64_t dOmn = smem_desc_sw128(smem_u32(sO), 8192, 1024);  // MN-major B of dV
       const uint64_t dSt = smem_desc_sw128(smem_u32(sSt), 16384, 1024); // MN-major A of dQ (buffer 0)
-      // S^T / dP^T of query half hf of tile t: M 128 keys, N 64 queries, into TMEM columns
-      // [64 hf, 64 hf + 64) and [128 + 64 hf, ...).
-      auto issue_sdp = [&](int t, int hf) {
-        const uint32_t off = (t & 1) * kTileBytes + hf * 8192;
+      // S^T / dP^T of query half hf of ring tile g with K / V buffer kvb: M 128 keys, N 64
+      // queries, into TMEM columns [64 hf, 64 hf + 64) and [128 + 64 hf, ...).
+      auto issue_sdp = [&](uint32_t g, int hf, int kvb) {
+        const uint32_t off = (g & 1) * kTileBytes + hf * 8192;
+        const uint32_t kvo = kvb * 2 * kTileBytes;
         const uint64_t bq = desc_adv(dQk, off), bo = desc_adv(dOk, off);
+        const uint64_t ak = desc_adv(dK, kvo), av = desc_adv(dV, kvo);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          umma_f16(tmem + hf * 64, desc_adv(dK, kk * 32), desc_adv(bq, kk * 32), id_sq, kk > 0 ? 1u : 0u);
-          umma_f16(tmem + 128 + hf * 64, desc_adv(dV, kk * 32), desc_adv(bo, kk * 32), id_sq, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + hf * 64, desc_adv(ak, kk * 32), desc_adv(bq, kk * 32), id_sq, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 128 + hf * 64, desc_adv(av, kk * 32), desc_adv(bo, kk * 32), id_sq, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->sdp_full[hf]);
       };
-      bool ok = wait(&bars->kv_full, 0, abort_flag, status, kFaMma) &&
-                wait(&bars->q_full[0], 0, abort_flag, status, kFaMma);
-      if (ok) {
-        tc_fence_after();
-        issue_sdp(0, 0);
-        issue_sdp(0, 1);
-      }
-      for (int t = 0; t < ntiles && ok; ++t) {
-        const int s = t & 1;
-        const uint64_t bq = desc_adv(dQmn, s * kTileBytes), bo = desc_adv(dOmn, s * kTileBytes);
-        for (int hf = 0; hf < 2 && ok; ++hf) {
-          // P^T / dS^T of this half are in TMEM (over its S^T / dP^T columns).
-          if (!(ok = wait(&bars->p_full[hf], t & 1, abort_flag, status, kFaMma))) break;
+      uint32_t g = 0;  // query tiles processed (ring slot and TMEM / shared buffer parities)
+      bool ok = true;
+      int idx = ring_take(&bars->items, 0, abort_flag, status, kFaMma);
+      if (idx >= 0 && idx < total) {
+        ok = wait(&bars->kv_full[0], 0, abort_flag, status, kFaMma) &&
+             wait(&bars->q_full[0], 0, abort_flag, status, kFaMma);
+        if (ok) {
           tc_fence_after();
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int kk = hf * 4 + j;  // 16 queries per step
-            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-            umma_f16_ts(tmem + 256, tmem + pair_col(kk), desc_adv(bo, kk * 2048), id_kn, acc);
-            umma_f16_ts(tmem + 320, tmem + 128 + pair_col(kk), desc_adv(bq, kk * 2048), id_kn, acc);
-          }
-          if (hf == 1) umma_commit(&bars->q_empty[s]);  // Q_t / dO_t are no longer read
-          // The next tile's scores of this half overwrite the columns dV / dK just read; the
-          // tensor core runs a thread's products in issue order.
-          if (t + 1 < ntiles) {
-            if (hf == 0 && !(ok = wait(&bars->q_full[(t + 1) & 1], ((t + 1) >> 1) & 1, abort_flag, status, kFaMma)))
+          issue_sdp(0, 0, 0);
+          issue_sdp(0, 1, 0);
+        }
+      }
+      for (uint32_t n = 0; ok && idx >= 0 && idx < total; ++n) {
+        const BwdItem it = bwd_decode(idx, nqb, H, B);
+        const int ntiles = nqb - it.kb;
+        const int kvb = n & 1;
+        const uint64_t kmn = desc_adv(dKmn, kvb * 2 * kTileBytes);
+        int next = -1;  // the following item, taken during this item's last tile
+        for (int t = 0; t < ntiles && ok; ++t, ++g) {
+          const int s = g & 1;
+          const uint64_t bq = desc_adv(dQmn, s * kTileBytes), bo = desc_adv(dOmn, s * kTileBytes);
+          for (int hf = 0; hf < 2 && ok; ++hf) {
+            // P^T / dS^T of this half are in TMEM (over its S^T / dP^T columns).
+            if (!(ok = wait(&bars->p_full[hf], g & 1, abort_flag, status, kFaMma))) break;
+            // The first dV / dK products of an item overwrite the accumulators: the previous
+            // item's epilogue has read them.
+            if (t == 0 && hf == 0 && n > 0 && !(ok = wait(&bars->acc_drained, (n - 1) & 1, abort_flag, status, kFaMma)))
               break;
-            issue_sdp(t + 1, hf);
-          }
-        }
-        if (!ok) break;
-        if (!(ok = wait(&bars->dq_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, status, kFaMma))) break;
-        tc_fence_after();
-        const uint64_t sbuf = desc_adv(dSt, s * kPBytes);
+            tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          // dS^T read MN-major: queries contiguous (two 64-query halves 16 KiB apart), 16 keys per step.
-          umma_f16(tmem + 384 + (t & 1) * D, desc_adv(sbuf, kk * 2048), desc_adv(dKmn, kk * 2048), id_q,
-                   kk > 0 ? 1u : 0u);
+            for (int j = 0; j < 4; ++j) {
+              const int kk = hf * 4 + j;  // 16 queries per step
+              const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+              umma_f16_ts(tmem + 256, tmem + pair_col(kk), desc_adv(bo, kk * 2048), id_kn, acc);
+              umma_f16_ts(tmem + 320, tmem + 128 + pair_col(kk), desc_adv(bq, kk * 2048), id_kn, acc);
+            }
+            if (hf == 1) umma_commit(&bars->q_empty[s]);  // Q / dO / LSE / Delta of this slot are no longer read
+            // The next tile's scores of this half overwrite the columns dV / dK just read; the
+            // tensor core runs a thread's products in issue order.
+            if (t + 1 < ntiles) {
+              if (hf == 0) {
+                if (!(ok = wait(&bars->q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma))) break;
+                tc_fence_after();
+              }
+              issue_sdp(g + 1, hf, kvb);
+            } else {
+              if (hf == 0) {
+                next = ring_take(&bars->items, n + 1, abort_flag, status, kFaMma);
+                if (next < 0) {
+                  ok = false;
+                  break;
+                }
+                if (next < total) {
+                  if (!(ok = wait(&bars->kv_full[kvb ^ 1], ((n + 1) >> 1) & 1, abort_flag, status, kFaMma) &&
+                             wait(&bars->q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma)))
+                    break;
+                  tc_fence_after();
+                }
+              }
+              if (next < total) issue_sdp(g + 1, hf, kvb ^ 1);  // the next item's first tile
+            }
+          }
+          if (!ok) break;
+          if (!(ok = wait(&bars->dq_free[g & 1], ((g >> 1) & 1) ^ 1, abort_flag, status, kFaMma))) break;
+          tc_fence_after();
+          const uint64_t sbuf = desc_adv(dSt, s * kPBytes);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            // dS^T read MN-major: queries contiguous (two 64-query halves 16 KiB apart), 16 keys per step.
+            umma_f16(tmem + 384 + (g & 1) * D, desc_adv(sbuf, kk * 2048), desc_adv(kmn, kk * 2048), id_q,
+                     kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars->grads_done);
+          if (t + 1 == ntiles) umma_commit(&bars->kv_empty[kvb]);  // K / V of this item are no longer read
         }
-        umma_commit(&bars->grads_done);
+        idx = next;
       }
     }
   } else {
     const int quarter = warp & 3;         // TMEM lane quarter
     const int colh = (warp - 2) >> 2;     // which half of the query columns
     const int r = quarter * 32 + lane;    // key row (S^T / dP^T / dK / dV) or query row (dQ)
-    const int key = kb * BKV + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    // dQ of query tile tp: TMEM lanes are query rows; this warp adds 32 of the 64 columns,
-    // staged in shared memory and added to the fp32 accumulator by one TMA reduce.
+    // dQ of ring tile gp: TMEM lanes are query rows; this warp adds 32 of the 64 columns of its
+    // 32 rows (from global row qrow) to the fp32 accumulator: two 16-column halves, each staged in
+    // shared memory (64B swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3)) and added by one
+    // TMA reduce.
     uint8_t* dq_stage = sDq + (warp - 2) * kDqStageBytes;
-    auto drain_dq = [&](int tp) {
-      const int buf = tp & 1;
+    auto drain_dq = [&](uint32_t gp, int head, int qrow) {
+      const int buf = gp & 1;
       tc_fence_after();
       uint32_t qr[32];
       tmem_ld32(lane_base + 384 + buf * D + colh * 32, qr);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars->dq_free[buf]);
-        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // previous reduce has read the staging
-      }
-      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->dq_free[buf]);
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(dq_stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-            make_uint4(qr[c * 4], qr[c * 4 + 1], qr[c * 4 + 2], qr[c * 4 + 3]);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        asm volatile(
-            "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                reinterpret_cast<uint64_t>(&tm_dq)),
-            "r"(smem_u32(dq_stage)), "r"(h * D + colh * 32), "r"(row_base + (kb + tp) * BQ + quarter * 32)
-            : "memory");
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      for (int part = 0; part < 2; ++part) {
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the staging was read
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int w = part * 16 + c * 4;
+          *reinterpret_cast<uint4*>(dq_stage + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(qr[w], qr[w + 1], qr[w + 2], qr[w + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          asm volatile(
+              "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                  reinterpret_cast<uint64_t>(&tm_dq)),
+              "r"(smem_u32(dq_stage)), "r"(head * D + colh * 32 + part * 16), "r"(qrow)
+              : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
       }
     };
-    bool ok = true;
     uint8_t* srow0 = sSt + colh * 16384 + (r >> 3) * 1024 + (r & 7) * 128;  // this thread's dS^T row
-    for (int t = 0; t < ntiles && ok; ++t) {
-      const int s = t & 1, qi = kb + t;
-      const bool diag = (t == 0);
-      if (!wait(&bars->q_full[s], (t >> 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
-      if (!warp_wait(&bars->sdp_full[colh], t & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
-      uint8_t* srow = srow0 + s * kPBytes;
-      tc_fence_after();
-      const float* Ls = sL + s * BQ;
-      const float* Ds = sD + s * BQ;
-      const int lim = diag ? key - qi * BQ : -1;  // on the diagonal tile, queries at index < lim are masked
-      // The diagonal tile masks queries before this thread's key; the other tiles compile without the test.
-      auto softmax_tile = [&](auto diag_tag) {
-        constexpr bool kDiag = decltype(diag_tag)::value;
-  #pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          // 32 queries: S^T / dP^T in, P^T / dS^T (fp16 pairs) back over the first 16 columns of
-          // this warp's half (already read), dS^T also to shared memory.
-          const int q0 = colh * 64 + ch * 32;
-          uint32_t sr[32], dr[32];
-          tmem_ld32(lane_base + q0, sr);
-          tmem_ld32(lane_base + 128 + q0, dr);
-          tmem_ld_wait();
-          uint32_t pw[16], sw[16];
-  #pragma unroll
-          for (int gq = 0; gq < 8; ++gq) {  // 4 queries per group: LSE / Delta as float4 (broadcast reads)
-            const float4 L4 = *reinterpret_cast<const float4*>(Ls + q0 + gq * 4);
-            const float4 D4 = *reinterpret_cast<const float4*>(Ds + q0 + gq * 4);
-            const float nl[4] = {L4.x, L4.y, L4.z, L4.w};
-            const float dl[4] = {D4.x, D4.y, D4.z, D4.w};
-            float pv[4], dv[4];
-  #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int qc = gq * 4 + u;
-              float p = ex2(fmaf(__uint_as_float(sr[qc]), scale_log2, nl[u]));
-              if (kDiag && q0 + qc < lim) p = 0.f;
-              pv[u] = p;
-              dv[u] = p * (__uint_as_float(dr[qc]) - dl[u]);
+    uint32_t g = 0;
+    bool ok = true;
+    for (uint32_t n = 0; ok; ++n) {
+      const int idx = ring_take_warp(&bars->items, n, abort_flag, status, kFaSoftmax);
+      if (idx < 0) break;
+      if (idx >= total) break;
+      const BwdItem it = bwd_decode(idx, nqb, H, B);
+      const int ntiles = nqb - it.kb;
+      const int key = it.kb * BKV + r;
+      const int row_base = it.b * T;
+      const int dq_row0 = row_base + quarter * 32;  // + qi * BQ: this warp's first dQ row of tile qi
+      for (int t = 0; t < ntiles && ok; ++t, ++g) {
+        const int s = g & 1, qi = it.kb + t;
+        const bool diag = (t == 0);
+        if (!wait(&bars->q_full[s], (g >> 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+        if (!warp_wait(&bars->sdp_full[colh], g & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+        uint8_t* srow = srow0 + s * kPBytes;
+        tc_fence_after();
+        const float* Ls = sL + s * BQ;
+        const float* Ds = sD + s * BQ;
+        const int lim = diag ? key - qi * BQ : -1;  // on the diagonal tile, queries at index < lim are masked
+        // The diagonal tile masks queries before this thread's key; the other tiles compile without the test.
+        auto softmax_tile = [&](auto diag_tag) {
+          constexpr bool kDiag = decltype(diag_tag)::value;
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            // 32 queries: S^T / dP^T in, P^T / dS^T (fp16 pairs) back over the first 16 columns of
+            // this warp's half (already read), dS^T also to shared memory.
+            const int q0 = colh * 64 + ch * 32;
+            uint32_t sr[32], dr[32];
+            tmem_ld32(lane_base + q0, sr);
+            tmem_ld32(lane_base + 128 + q0, dr);
+            tmem_ld_wait();
+            uint32_t pw[16], sw[16];
+#pragma unroll
+            for (int gq = 0; gq < 8; ++gq) {  // 4 queries per group: -LSE log2(e) / Delta as float4 (broadcast reads)
+              const float4 L4 = *reinterpret_cast<const float4*>(Ls + q0 + gq * 4);
+              const float4 D4 = *reinterpret_cast<const float4*>(Ds + q0 + gq * 4);
+              const float nl[4] = {L4.x, L4.y, L4.z, L4.w};
+              const float dl[4] = {D4.x, D4.y, D4.z, D4.w};
+              float pv[4], dv[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int qc = gq * 4 + u;
+                float p = ex2(fmaf(__uint_as_float(sr[qc]), scale_log2, nl[u]));
+                if (kDiag && q0 + qc < lim) p = 0.f;
+                pv[u] = p;
+                dv[u] = p * (__uint_as_float(dr[qc]) - dl[u]);
+              }
+              __half2 hp0 = __floats2half2_rn(pv[0], pv[1]), hp1 = __floats2half2_rn(pv[2], pv[3]);
+              __half2 hs0 = __floats2half2_rn(dv[0], dv[1]), hs1 = __floats2half2_rn(dv[2], dv[3]);
+              pw[gq * 2] = *reinterpret_cast<uint32_t*>(&hp0);
+              pw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hp1);
+              sw[gq * 2] = *reinterpret_cast<uint32_t*>(&hs0);
+              sw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hs1);
             }
-            __half2 hp0 = __floats2half2_rn(pv[0], pv[1]), hp1 = __floats2half2_rn(pv[2], pv[3]);
-            __half2 hs0 = __floats2half2_rn(dv[0], dv[1]), hs1 = __floats2half2_rn(dv[2], dv[3]);
-            pw[gq * 2] = *reinterpret_cast<uint32_t*>(&hp0);
-            pw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hp1);
-            sw[gq * 2] = *reinterpret_cast<uint32_t*>(&hs0);
-            sw[gq * 2 + 1] = *reinterpret_cast<uint32_t*>(&hs1);
+            tmem_st16(lane_base + colh * 64 + ch * 16, pw);
+            tmem_st16(lane_base + 128 + colh * 64 + ch * 16, sw);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {  // 4 chunks of 8 queries
+              const int off = ((ch * 4 + c) ^ (r & 7)) << 4;
+              *reinterpret_cast<uint4*>(srow + off) = make_uint4(sw[c * 4], sw[c * 4 + 1], sw[c * 4 + 2], sw[c * 4 + 3]);
+            }
           }
-          tmem_st16(lane_base + colh * 64 + ch * 16, pw);
-          tmem_st16(lane_base + 128 + colh * 64 + ch * 16, sw);
-  #pragma unroll
-          for (int c = 0; c < 4; ++c) {  // 4 chunks of 8 queries
-            const int off = ((ch * 4 + c) ^ (r & 7)) << 4;
-            *reinterpret_cast<uint4*>(srow + off) = make_uint4(sw[c * 4], sw[c * 4 + 1], sw[c * 4 + 2], sw[c * 4 + 3]);
-          }
+        };
+        if (diag)
+          softmax_tile(std::true_type{});
+        else
+          softmax_tile(std::false_type{});
+        tmem_st_wait();
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[colh]);
+        // The previous tile's dQ completed before this tile's scores; reduce it while this tile's products run.
+        if (t > 0) {
+          if (!warp_wait(&bars->grads_done, (g - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
+          drain_dq(g - 1, it.h, dq_row0 + (qi - 1) * BQ);
         }
-      };
-      if (diag)
-        softmax_tile(std::true_type{});
-      else
-        softmax_tile(std::false_type{});
-      tmem_st_wait();
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[colh]);
-      // The previous tile's dQ completed before this tile's scores; reduce it while this tile's products run.
-      if (t > 0) {
-        if (!warp_wait(&bars->grads_done, (t - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
-        drain_dq(t - 1);
       }
-    }
-    if (ok && !warp_wait(&bars->grads_done, (ntiles - 1) & 1, abort_flag, status, kFaSoftmax)) ok = false;
-    if (ok) drain_dq(ntiles - 1);
-    if (ok) {
-      // dK (warps with colh 0, scaled, rotated back through RoPE) and dV (colh 1).
+      if (!ok) break;
+      // The item's last dQ, then dK (warps with colh 0, scaled, rotated back through RoPE) and dV (colh 1).
+      if (!warp_wait(&bars->grads_done, (g - 1) & 1, abort_flag, status, kFaSoftmax)) break;
+      drain_dq(g - 1, it.h, dq_row0 + (nqb - 1) * BQ);
       tc_fence_after();
       uint32_t ar[64];
       const uint32_t col = colh == 0 ? 320u : 256u;
       tmem_ld32(lane_base + col, *reinterpret_cast<uint32_t(*)[32]>(&ar[0]));
       tmem_ld32(lane_base + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&ar[32]));
       tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_drained);  // the next item's first dV / dK products may overwrite them
       float v[64];
       const float sc = colh == 0 ? scale : 1.0f;
 #pragma unroll
@@ -764,7 +850,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int c = 0; c < 32; ++c) rope_back(v[c], v[c + 32], rope_cos, rope_sin, key, c);
       }
-      __half* dst = dqkv + (int64_t)(row_base + key) * (3 * d) + (colh == 0 ? d : 2 * d) + h * D;
+      __half* dst = dqkv + (int64_t)(row_base + key) * (3 * d) + (colh == 0 ? d : 2 * d) + it.h * D;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t w[4];
@@ -867,7 +953,8 @@ extern "C" int jx_attn_fwd(const void* qkv, void* out, float* lse, void* workspa
 }
 
 extern "C" int64_t jx_attn_bwd_workspace_bytes(int B, int T, int H, int Dh) {
-  return 2 * (int64_t)B * H * T * 4 + (int64_t)B * T * H * Dh * 4;  // Delta, -LSE log2(e), dQ accumulator
+  // Delta, -LSE log2(e), the fp32 dQ accumulator, the work counter of the persistent kernel.
+  return 2 * (int64_t)B * H * T * 4 + (int64_t)B * T * H * Dh * 4 + 256;
 }
 
 // Delta = rowsum(dO * O), computed by attn_delta_kernel in attention.cu.
@@ -897,10 +984,14 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
   CUtensorMap tq, tdo;
   JX_CHECK_ARG(make_tmap_f16(&tq, qkv, 3LL * d, rows, 3LL * d, D, BKV), "jx_attn_bwd: cannot encode TMA descriptor");
   JX_CHECK_ARG(make_tmap_f16(&tdo, dout, d, rows, d, D, BQ), "jx_attn_bwd: cannot encode TMA descriptor");
+  int* counter = reinterpret_cast<int*>(dq_acc + rows * d);
   CUtensorMap tdq;
-  JX_CHECK_ARG(make_tmap_f32(&tdq, dq_acc, d, rows, d, 32, 32),
+  JX_CHECK_ARG(make_tmap_f32(&tdq, dq_acc, d, rows, d, 16, 32, 64),
                "jx_attn_bwd: cannot encode TMA descriptor for the dQ accumulator");
-  JX_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)rows * d * sizeof(float), s), "jx_attn_bwd: clear dq accumulator");
+  JX_CHECK_ARG((int64_t)(T / BQ) * H * B < (1LL << 30), "jx_attn_bwd: too many work items");
+  // One clear for the dQ accumulator and the work counter behind it.
+  JX_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)rows * d * sizeof(float) + sizeof(int), s),
+              "jx_attn_bwd: clear dq accumulator");
   jx::attn::launch_delta(static_cast<const __half*>(out), static_cast<const __half*>(dout), lse, delta, nl2, B, T, H, s);
   JX_CHECK_LAUNCH("jx_attn_bwd: delta");
   static bool attr_set = false;
@@ -909,10 +1000,11 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
                 "jx_attn_bwd: smem attribute");
     attr_set = true;
   }
-  dim3 grid(T / BKV, H, B);
-  attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, tdq, nl2, delta, dq_acc, static_cast<__half*>(dqkv), T, H,
-                                                        scale, scale * 1.4426950408889634f, rope_cos, rope_sin,
-                                                        status_ptr());
+  const int64_t items = (int64_t)(T / BQ) * H * B;
+  const int grid = (int)std::min<int64_t>(items, num_sms());
+  attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, tdq, nl2, delta, dq_acc, static_cast<__half*>(dqkv),
+                                                        counter, B, T, H, scale, scale * 1.4426950408889634f,
+                                                        rope_cos, rope_sin, status_ptr());
   JX_CHECK_LAUNCH("jx_attn_bwd");
   const int64_t groups = rows * H * 4;
   attn_dq_finish_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, s>>>(dq_acc, static_cast<__half*>(dqkv), rows, H, T,

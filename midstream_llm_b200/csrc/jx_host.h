@@ -24,8 +24,8 @@ enum DeviceStatus : int {
 bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
                    uint32_t box_inner, uint32_t box_outer);
 
-// The same for fp32 tensors (box_inner * 4 bytes <= 128).
+// The same for fp32 tensors (box_inner * 4 bytes <= swizzle_bytes; 128- or 64-byte swizzle).
 bool make_tmap_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
-                   uint32_t box_inner, uint32_t box_outer);
+                   uint32_t box_inner, uint32_t box_outer, int swizzle_bytes = 128);
 
 }  // namespace jx
