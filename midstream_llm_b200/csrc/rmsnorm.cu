@@ -190,22 +190,29 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __half* 
   }
 }
 
-// dgamma[c] (+)= sum_p part[p][c]: 32 columns x 8 part-groups per block,
-// deterministic order (fixed partition, fixed tree).
-__global__ void __launch_bounds__(256) dgamma_reduce_kernel(const float* __restrict__ part, int nparts, int cols,
-                                                            float* __restrict__ dgamma, int accumulate) {
-  __shared__ float red[8][33];
+// dgamma[c] (+)= sum_p part[p][c]: 32 columns x 32 part-groups per block (each thread sums
+// every 32nd part with two independent accumulators, so its loads overlap), then a fixed tree
+// over the groups: deterministic order.
+__global__ void __launch_bounds__(1024) dgamma_reduce_kernel(const float* __restrict__ part, int nparts, int cols,
+                                                             float* __restrict__ dgamma, int accumulate) {
+  __shared__ float red[32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + tx;
-  float s = 0.f;
-  if (c < cols)
-    for (int p = ty; p < nparts; p += 8) s += part[(int64_t)p * cols + c];
-  red[ty][tx] = s;
+  float s0 = 0.f, s1 = 0.f;
+  if (c < cols) {
+    int p = ty;
+    for (; p + 32 < nparts; p += 64) {
+      s0 += part[(int64_t)p * cols + c];
+      s1 += part[(int64_t)(p + 32) * cols + c];
+    }
+    if (p < nparts) s0 += part[(int64_t)p * cols + c];
+  }
+  red[ty][tx] = s0 + s1;
   __syncthreads();
   if (ty == 0 && c < cols) {
     float t = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) t += red[j][tx];
+    for (int j = 0; j < 32; ++j) t += red[j][tx];
     dgamma[c] = accumulate ? dgamma[c] + t : t;
   }
 }
@@ -299,7 +306,7 @@ extern "C" int jx_rmsnorm_bwd(const void* dy, const void* x, const float* rstd, 
 extern "C" int jx_rmsnorm_dgamma_reduce(const float* dgamma_part, int nparts, int cols, float* dgamma, int accumulate,
                                         jx_stream_t stream) {
   JX_CHECK_ARG(dgamma_part && dgamma && nparts > 0 && cols > 0, "jx_rmsnorm_dgamma_reduce: bad argument");
-  dgamma_reduce_kernel<<<(cols + 31) / 32, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  dgamma_reduce_kernel<<<(cols + 31) / 32, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       dgamma_part, nparts, cols, dgamma, accumulate);
   JX_CHECK_LAUNCH("jx_rmsnorm_dgamma_reduce");
   return JX_OK;
@@ -385,7 +392,7 @@ extern "C" int jx_rmsnorm_bwd_noalloc(const void* dy, const void* x, const float
       return JX_ERR_UNSUPPORTED;
   }
   JX_CHECK_LAUNCH("jx_rmsnorm_bwd_noalloc");
-  dgamma_reduce_kernel<<<(cols + 31) / 32, 256, 0, s>>>(part, grid, cols, dgamma, accumulate);
+  dgamma_reduce_kernel<<<(cols + 31) / 32, 1024, 0, s>>>(part, grid, cols, dgamma, accumulate);
   JX_CHECK_LAUNCH("jx_rmsnorm_bwd_noalloc: reduce");
   return JX_OK;
 }
