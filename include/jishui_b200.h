@@ -139,7 +139,9 @@ int jx_gemm_swiglu_bwd(const void* dY, int64_t lddy, const void* Wd, int M, int 
  * dY f16 [T, N], X f16 [T, K], G f32 [N, K] (leading dimension ldg).
  * The product is rounded to f16 before it is added, as an fp16 autocast
  * Linear's weight gradient is. `splits` > 1 splits the T reduction across
- * CTAs; it needs `workspace` of jx_gemm_wgrad_workspace_bytes(N, K, splits). */
+ * CTAs, whose fp32 partials are added into one accumulator (zeroed by the call)
+ * before the f16 rounding; it needs `workspace` of
+ * jx_gemm_wgrad_workspace_bytes(N, K, splits) = N*K*4 bytes. */
 int64_t jx_gemm_wgrad_workspace_bytes(int N, int K, int splits);
 /* Kernel choice for all GEMM entry points: 0 (default) runs the 2-SM
  * kernel (a CTA pair per 256 x 256 tile, tcgen05 cta_group::2) whenever M

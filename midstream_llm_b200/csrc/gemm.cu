@@ -236,6 +236,25 @@ struct Stager {
       bulk_commit();
     }
   }
+  // 32 fp32 values of this lane's row (a 32 x 32 fp32 box, 128B-swizzled).
+  __device__ __forceinline__ void put_f32(const float (&v)[32]) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  }
+  // Adds the staged box to global memory (TMA reduce-add; out-of-range rows / columns are clipped).
+  __device__ __forceinline__ void flush_add(const CUtensorMap* map, int x, int y) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                       reinterpret_cast<uint64_t>(map)),
+                   "r"(smem_u32(buf)), "r"(x), "r"(y)
+                   : "memory");
+      bulk_commit();
+    }
+  }
 };
 
 // Per-warp TMA staging of the epilogue's row-wise inputs (gate and up boxes of 32 rows x 64
@@ -312,18 +331,24 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
         st.put32(1, v1);
         st.flush(om.c0, col0, yrow);
       } else {
+        if (p.splits > 1) {
+          // Split-K: this split's fp32 partial is added into the one shared workspace by TMA reduce-add
+          // (32 x 32 boxes through the warp's staging buffer), so the partial sums meet in L2.
+          (void)split;
+#pragma unroll
+          for (int part = 0; part < 2; ++part) {
+            st.begin();
+            st.put_f32(part ? v1 : v0);
+            st.flush_add(om.c0, col0 + part * 32, yrow);
+          }
+          continue;
+        }
         if (row >= p.M) continue;
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
           const int col = col0 + part * 32;
           const float* v = part ? v1 : v0;
-          if (p.splits > 1) {
-            float* dst = p.ws + ((int64_t)split * p.M + row) * p.N + col;
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              if (col + g * 4 + 4 <= p.N)
-                *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
-          } else {
+          {
             float* dst = p.G + (int64_t)row * p.ldg + col;
             float vr[32];
 #pragma unroll
@@ -944,23 +969,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Split-K reduction for the weight gradient: G (+)= f32(f16(sum_s ws[s])).
-__global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, float* __restrict__ G,
-                                    int64_t ldg, int accumulate) {
+// Split-K finish for the weight gradient: G (+)= f32(f16(ws)), ws holding the sum of every split's
+// partial (added by the splits' TMA reduces into the zeroed workspace).
+__global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int M, int N, float* __restrict__ G, int64_t ldg,
+                                    int accumulate) {
   const int64_t total4 = (int64_t)M * N / 4;
-  const int64_t plane = (int64_t)M * N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total4; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i * 4;
     const int row = (int)(e / N);
     const int col = (int)(e - (int64_t)row * N);
-    float4 acc = *reinterpret_cast<const float4*>(ws + e);
-    for (int s = 1; s < splits; ++s) {
-      float4 v = *reinterpret_cast<const float4*>(ws + s * plane + e);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
-    }
+    const float4 acc = *reinterpret_cast<const float4*>(ws + e);
     float* dst = G + (int64_t)row * ldg + col;
     float4 o = make_float4(h2f_round(acc.x), h2f_round(acc.y), h2f_round(acc.z), h2f_round(acc.w));
     if (accumulate) {
@@ -1179,6 +1197,9 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
     ok = make_tmap_f16(&tc0, p.C, p.swiglu_F, p.M, p.ldc, 64, 32) &&
          make_tmap_f16(&tc1, p.C + p.swiglu_F, p.swiglu_F, p.M, p.ldc, 64, 32);
   }
+  if constexpr (EPI == kWgrad) {
+    if (p.splits > 1) ok = make_tmap_f32(&tc0, p.ws, p.N, p.M, p.N, 32, 32);
+  }
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for the output", name);
   // The SwiGLU-backward epilogue's gate / up inputs, read as 32 x 64 boxes.
   CUtensorMap tx0 = tc0, tx1 = tc0;
@@ -1339,7 +1360,7 @@ extern "C" int jx_gemm_swiglu_bwd(const void* dY, int64_t lddy, const void* Wd, 
 
 extern "C" int64_t jx_gemm_wgrad_workspace_bytes(int N, int K, int splits) {
   if (splits <= 1) return 0;
-  return (int64_t)splits * N * K * (int64_t)sizeof(float);
+  return (int64_t)N * K * (int64_t)sizeof(float);  // one fp32 accumulator, whatever the split count
 }
 
 extern "C" int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_t ldx, int T, int N, int K, float* G,
@@ -1362,12 +1383,14 @@ extern "C" int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_
   const int per = (num_kb + sp - 1) / sp;
   sp = (num_kb + per - 1) / per;
   p.splits = sp;
+  if (sp > 1)
+    JX_CUDA_TRY(cudaMemsetAsync(workspace, 0, (size_t)N * K * sizeof(float), s), "jx_gemm_wgrad: clear workspace");
   int rc = launch<kWgrad, true, true>(dY, lddy, X, ldx, p, s, "jx_gemm_wgrad");
   if (rc != JX_OK || sp == 1) return rc;
   const int64_t total4 = (int64_t)N * K / 4;
   int blocks = (int)((total4 + 255) / 256);
   if (blocks > num_sms() * 8) blocks = num_sms() * 8;
-  wgrad_reduce_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(workspace), sp, N, K, G, ldg, accumulate);
+  wgrad_reduce_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(workspace), N, K, G, ldg, accumulate);
   JX_CHECK_LAUNCH("jx_gemm_wgrad: reduce");
   return JX_OK;
 }

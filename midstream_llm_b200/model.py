@@ -266,8 +266,9 @@ class Workspace:
 def _wgrad_splits(n: int, k: int, tokens: int = 16384, pairs: int = 74) -> int:
     """Split count for a weight-gradient GEMM with [n, k] output reducing over
     `tokens`, for the 2-SM kernel (a CTA pair per 256 x 256 tile, `pairs` pairs
-    resident): minimises (waves x per-split main loop) + the split-K partials'
-    HBM round trip, at ~14.8 TFLOP/s per pair and 6 TB/s."""
+    resident): minimises (waves x per-split main loop) + the split-K cost (clearing
+    and reading back the one fp32 accumulator, the splits' reduce-adds in L2), at
+    ~14.8 TFLOP/s per pair and 6 TB/s."""
     tiles = -(-n // 256) * -(-k // 256)
     tile_us = 2.0 * 256 * 256 * tokens / 14.8e6  # one tile over all tokens, microseconds
     best, best_t = 1, None
@@ -276,7 +277,7 @@ def _wgrad_splits(n: int, k: int, tokens: int = 16384, pairs: int = 74) -> int:
             break
         t = math.ceil(tiles * s / pairs) * tile_us / s
         if s > 1:
-            t += (2.0 * s + 2.0) * n * k * 4 / 6e6
+            t += (2.0 + 0.25 * s) * n * k * 4 / 6e6
         if best_t is None or t < best_t * 0.97:
             best, best_t = s, t
     return best
