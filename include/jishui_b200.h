@@ -25,7 +25,8 @@
  *   src/jishui/model_torch.py:59-60   SwiGLU                -> jx_gemm_swiglu_fwd / jx_gemm_swiglu_bwd
  *   src/jishui/model_torch.py:89-93   nn.Embedding + cast   -> jx_embed_fwd / jx_embed_bwd
  *   src/jishui/model_torch.py:98      tied head F.linear    -> jx_gemm_f16 (+ jx_gemm_wgrad for dE)
- *   src/jishui/model_torch.py:102-104 F.cross_entropy(logits.float()) -> jx_ce_fwd / jx_ce_loss / jx_ce_bwd
+ *   src/jishui/model_torch.py:102-104 F.cross_entropy(logits.float()) -> jx_ce_fwd (or jx_gemm_f16_ce_parts +
+ *                                     jx_ce_fwd_parts) / jx_ce_loss / jx_ce_bwd
  *   src/jishui/pretrain_torch.py:218-219 GradScaler.unscale_ + clip_grad_norm_ -> jx_grad_stats / jx_grad_finalize
  *   src/jishui/pretrain_torch.py:119-120,231 AdamW(fused=True).step -> jx_adamw_step
  */
@@ -196,6 +197,14 @@ int jx_pack_rows(const void* tokens, int64_t ntokens, const int64_t* runs, const
  * target == ignore_index give loss 0 and are excluded from the mean. */
 int jx_ce_fwd(const void* logits16, int64_t rows, int vocab, int64_t ld, const int64_t* targets, int64_t ignore_index,
               float* lse, float* row_loss, jx_stream_t stream);
+/* The tied head with the cross-entropy statistics in its epilogue: C = A B^T as jx_gemm_f16 (A [M, K],
+ * B [N, K], both K-major, no residual) and parts [M][ceil(N/128)] of float pairs (max, sum exp(v - max))
+ * over each 128-column block of the f16 logits v. jx_ce_fwd_parts then gives what jx_ce_fwd gives without
+ * reading the logits again (nblk = ceil(vocab / 128); only the target logit is read). */
+int jx_gemm_f16_ce_parts(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, void* C,
+                         int64_t ldc, void* parts, jx_stream_t stream);
+int jx_ce_fwd_parts(const void* parts, int nblk, const void* logits16, int64_t rows, int vocab, int64_t ld,
+                    const int64_t* targets, int64_t ignore_index, float* lse, float* row_loss, jx_stream_t stream);
 /* loss_sum_count[0] = sum of row losses, [1] = number of counted rows,
  * [2] = [0]/[1], the mean loss (deterministic order); accumulate != 0 adds
  * to the existing sum and count. The buffer holds 3 floats. */

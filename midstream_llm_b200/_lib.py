@@ -43,6 +43,8 @@ _SIGNATURES: dict[str, tuple] = {
     "jx_attn_bwd_workspace_bytes": (c_int64, [c_int, c_int, c_int, c_int]),
     "jx_attn_bwd": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_float, _P, _P, _P]),
     "jx_ce_fwd": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int64, _P, _P, _P]),
+    "jx_gemm_f16_ce_parts": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P, c_int64, _P, _P]),
+    "jx_ce_fwd_parts": (c_int, [_P, c_int, _P, c_int64, c_int, c_int64, _P, c_int64, _P, _P, _P]),
     "jx_ce_loss": (c_int, [_P, _P, c_int64, c_int64, _P, c_int, _P]),
     "jx_ce_bwd": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int64, _P, _P, _P, _P]),
     "jx_grad_stats_parts": (c_int, [c_int64]),

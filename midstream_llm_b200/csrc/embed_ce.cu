@@ -103,6 +103,40 @@ __global__ void ce_fwd_kernel(const __half* __restrict__ logits, int64_t rows, i
   }
 }
 
+// The same statistics from per-block partials: the head GEMM (kHeadCE epilogue) leaves, for every row and
+// 128-column block b, (m_b, s_b) = (max, sum exp(v - m_b)) of the fp16 logits; one warp per row merges them
+// (lse = M + log sum_b s_b exp(m_b - M)) and reads the target's logit, so the logits are not read again.
+__global__ void ce_fwd_parts_kernel(const float2* __restrict__ parts, int nblk, const __half* __restrict__ logits,
+                                    int64_t rows, int vocab, int64_t ld, const int64_t* __restrict__ targets,
+                                    int64_t ignore_index, float* __restrict__ lse, float* __restrict__ row_loss) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float2* pr = parts + row * nblk;
+  float m = -INFINITY, s = 0.f;
+  for (int b = lane; b < nblk; b += 32) {
+    const float2 q = pr[b];
+    if (q.y == 0.f) continue;
+    const float nm = fmaxf(m, q.x);
+    s = (m == -INFINITY ? 0.f : s * expf(m - nm)) + q.y * expf(q.x - nm);
+    m = nm;
+  }
+  const float gm = warp_max(m);
+  s = (m == -INFINITY) ? 0.f : s * expf(m - gm);
+  s = warp_sum(s);
+  if (lane == 0) {
+    const float l = gm + logf(s);
+    lse[row] = l;
+    const int64_t t = targets[row];
+    float loss = 0.f;
+    if (t != ignore_index) {
+      const int64_t tc = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+      loss = l - __half2float(logits[row * ld + tc]);
+    }
+    row_loss[row] = loss;
+  }
+}
+
 // Deterministic single-block sum of the per-row losses and of counted rows.
 __global__ void ce_loss_kernel(const float* __restrict__ row_loss, const int64_t* __restrict__ targets,
                                int64_t ignore_index, int64_t rows, float* __restrict__ out, int accumulate) {
@@ -204,6 +238,20 @@ extern "C" int jx_ce_fwd(const void* logits16, int64_t rows, int vocab, int64_t 
   ce_fwd_kernel<<<grid, kWarps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(logits16), rows, vocab, ld, targets, ignore_index, lse, row_loss);
   JX_CHECK_LAUNCH("jx_ce_fwd");
+  return JX_OK;
+}
+
+extern "C" int jx_ce_fwd_parts(const void* parts, int nblk, const void* logits16, int64_t rows, int vocab, int64_t ld,
+                               const int64_t* targets, int64_t ignore_index, float* lse, float* row_loss,
+                               jx_stream_t stream) {
+  JX_CHECK_ARG(parts && logits16 && targets && lse && row_loss && rows > 0 && vocab > 0 && nblk == (vocab + 127) / 128,
+               "jx_ce_fwd_parts: bad argument (nblk must be ceil(vocab / 128))");
+  JX_CHECK_ARG(((uintptr_t)parts & 7) == 0, "jx_ce_fwd_parts: parts must be 8-byte aligned");
+  const unsigned grid = (unsigned)((rows + kWarps - 1) / kWarps);
+  ce_fwd_parts_kernel<<<grid, kWarps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float2*>(parts), nblk, static_cast<const __half*>(logits16), rows, vocab, ld, targets,
+      ignore_index, lse, row_loss);
+  JX_CHECK_LAUNCH("jx_ce_fwd_parts");
   return JX_OK;
 }
 

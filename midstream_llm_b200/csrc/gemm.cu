@@ -16,6 +16,8 @@
 //
 // Fused epilogues (reference call sites in Midstream-LLM):
 //   kF16      plain / residual add         model_torch.py:49,60,72-73,98
+//   kHeadCE   tied head (plain fp16 logits) + per-(row, 128-column block) max and sum of exp of
+//             the fp16 logits, the partial statistics of F.cross_entropy (model_torch.py:102-104)
 //   kRope     q|k|v projection + RoPE      model_torch.py:18-25,41-44
 //   kSwigluF  gate|up projection + SwiGLU  model_torch.py:59-60
 //   kSwigluB  down dgrad + SwiGLU backward (autograd of model_torch.py:60)
@@ -45,7 +47,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kStageOutBytes = 32 * 128;  // one 32-row x 64-col fp16 output sub-tile per epilogue warp
 constexpr size_t kSmemBytes = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiWarps * kStageOutBytes + 256 /*barriers*/;
 
-enum Epi : int { kF16 = 0, kRope = 1, kSwigluF = 2, kSwigluB = 3, kWgrad = 4 };
+enum Epi : int { kF16 = 0, kRope = 1, kSwigluF = 2, kSwigluB = 3, kWgrad = 4, kHeadCE = 5 };
 
 struct Params {
   int M, N, K;
@@ -66,6 +68,8 @@ struct Params {
   const float* rope_sin;
   int rope_seq;
   int rope_cols;
+  float2* ce_parts;  // kHeadCE: [M][ce_nblk] (max, sum exp(v - max)) of each 128-column block
+  int ce_nblk;
   int rope_tma;  // kRope, 2-SM: cos / sin rows of a warp read as one TMA box each (rope_seq % 32 == 0)
   float* G;
   int64_t ldg;
@@ -172,6 +176,13 @@ __device__ __forceinline__ void store_row32_f16(__half* base, int64_t ld, int ro
       *reinterpret_cast<uint4*>(dst + g * 8) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void to_f32(const uint32_t (&r)[32], float (&v)[32]) {
@@ -295,7 +306,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
   const int row = mb * BM + quarter * 32 + lane;
   const int yrow = mb * BM + quarter * 32;  // first row of this warp's TMA boxes
   const uint32_t tl = tacc + (static_cast<uint32_t>(quarter * 32) << 16);
-  if constexpr (EPI == kF16 || EPI == kWgrad) {
+  if constexpr (EPI == kF16 || EPI == kHeadCE || EPI == kWgrad) {
+    float ce_m = -INFINITY, ce_s = 0.f;  // kHeadCE: running statistics of this thread's 128-column block
 #pragma unroll 1
     for (int cp = 0; cp < 2; ++cp) {
       const int c0 = half * 4 + cp * 2;  // first of two 32-column chunks
@@ -313,7 +325,30 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
       float v0[32], v1[32];
       to_f32(r0, v0);
       to_f32(r1, v1);
-      if constexpr (EPI == kF16) {
+      if constexpr (EPI == kHeadCE) {
+        // The logits are stored as fp16: the statistics are taken over the rounded values, columns past N
+        // (zero accumulators) excluded; sum exp(v - m) = sum 2^((v - m) log2 e).
+        round_all(v0);
+        round_all(v1);
+        const int nv0 = min(32, p.N - col0), nv1 = min(32, p.N - col0 - 32);
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < nv0) m = fmaxf(m, v0[i]);
+          if (i < nv1) m = fmaxf(m, v1[i]);
+        }
+        const float ml = m * kLog2e;
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < nv0) sum += ex2_approx(fmaf(v0[i], kLog2e, -ml));
+          if (i < nv1) sum += ex2_approx(fmaf(v1[i], kLog2e, -ml));
+        }
+        const float nm = fmaxf(ce_m, m);
+        ce_s = (ce_m == -INFINITY ? 0.f : ce_s * ex2_approx((ce_m - nm) * kLog2e)) + sum * ex2_approx((m - nm) * kLog2e);
+        ce_m = nm;
+      }
+      if constexpr (EPI == kF16 || EPI == kHeadCE) {
         if (p.resid) {
           float a[32], b[32];
           unpack32(q0, a);
@@ -371,6 +406,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
           }
         }
       }
+    }
+    if constexpr (EPI == kHeadCE) {
+      const int blk_col = nb * BN + half * 128;
+      if (row < p.M && blk_col < p.N) p.ce_parts[(int64_t)row * p.ce_nblk + blk_col / 128] = make_float2(ce_m, ce_s);
     }
   } else if constexpr (EPI == kRope) {
     const int pos = p.rope_seq > 0 ? row % p.rope_seq : 0;
@@ -1187,7 +1226,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for B", name);
   // Output descriptors: [rows, cols] fp16 boxes of 32 rows x 64 columns (one epilogue warp's sub-tile).
   CUtensorMap tc0 = ta, tc1 = ta, tc2 = ta;
-  if constexpr (EPI == kF16 || EPI == kRope) {
+  if constexpr (EPI == kF16 || EPI == kHeadCE || EPI == kRope) {
     ok = make_tmap_f16(&tc0, p.C, p.N, p.M, p.ldc, 64, 32);
   } else if constexpr (EPI == kSwigluF) {
     ok = make_tmap_f16(&tc0, p.C, p.swiglu_F, p.M, p.ld_out, 64, 32) &&
@@ -1301,6 +1340,19 @@ extern "C" int jx_gemm_f16(const void* A, int64_t lda, int a_mn_major, const voi
   if (!a_mn_major && b_mn_major) return launch<kF16, false, true>(A, lda, B, ldb, p, s, "jx_gemm_f16");
   if (a_mn_major && !b_mn_major) return launch<kF16, true, false>(A, lda, B, ldb, p, s, "jx_gemm_f16");
   return launch<kF16, true, true>(A, lda, B, ldb, p, s, "jx_gemm_f16");
+}
+
+extern "C" int jx_gemm_f16_ce_parts(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, void* C,
+                                    int64_t ldc, void* parts, jx_stream_t stream) {
+  JX_CHECK_ARG(C && aligned16(C) && ldc % 8 == 0 && N % 8 == 0,
+               "jx_gemm_f16_ce_parts: C must be 16B aligned, ldc%%8==0, N%%8==0");
+  JX_CHECK_ARG(parts && ((uintptr_t)parts & 7) == 0, "jx_gemm_f16_ce_parts: parts must be 8-byte aligned");
+  Params p = base_params(M, N, K);
+  p.C = static_cast<__half*>(C);
+  p.ldc = ldc;
+  p.ce_parts = static_cast<float2*>(parts);
+  p.ce_nblk = (N + 127) / 128;
+  return launch<kHeadCE, false, false>(A, lda, B, ldb, p, reinterpret_cast<cudaStream_t>(stream), "jx_gemm_f16_ce_parts");
 }
 
 extern "C" int jx_gemm_qkv_rope(const void* X, int64_t ldx, const void* W, int M, int hidden, int K, void* C,

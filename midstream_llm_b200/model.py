@@ -248,6 +248,7 @@ class Workspace:
     logits: torch.Tensor              # [M, V] fp16; overwritten in place by dlogits in backward
     ce_lse: torch.Tensor
     row_loss: torch.Tensor
+    ce_parts: torch.Tensor            # [M, ceil(V/128), 2] head-epilogue cross-entropy statistics
     dx: torch.Tensor
     dxmid: torch.Tensor
     dh: torch.Tensor
@@ -342,6 +343,7 @@ class JishuiForCausalLM(nn.Module):
             B=B, T=T, xs=torch.empty(xs_slots, M, d, **f16), acts=[acts() for _ in range(nslots)],
             hf=torch.empty(M, d, **f16), meanf=torch.empty(M, **f32), rstdf=torch.empty(M, **f32), logits=torch.empty(M, c.vocab_size, **f16),
             ce_lse=torch.empty(M, **f32), row_loss=torch.empty(M, **f32),
+            ce_parts=torch.empty(M, ops.ce_parts_blocks(c.vocab_size), 2, **f32),
             dx=torch.empty(M, d, **f16) if train else None, dxmid=torch.empty(M, d, **f16) if train else None,
             dh=torch.empty(M, d, **f16) if train else None, do=torch.empty(M, d, **f16) if train else None,
             dqkv=torch.empty(M, 3 * d, **f16) if train else None, dgu=torch.empty(M, 2 * F, **f16) if train else None,
@@ -411,7 +413,7 @@ class JishuiForCausalLM(nn.Module):
         ops.gemm_swiglu_fwd(A.h2, w["wgu"], F, gate=A.gate, up=A.up, act=A.act)
         ops.gemm_f16(A.act, w["wd"], resid=A.xmid, out=x_out)
 
-    def _trunk_fwd(self, ids: torch.Tensor, train: bool) -> Workspace:
+    def _trunk_fwd(self, ids: torch.Tensor, train: bool, ce: bool = False) -> Workspace:
         c = self.config
         B, T = ids.shape
         if T > c.max_position_embeddings:
@@ -433,7 +435,10 @@ class JishuiForCausalLM(nn.Module):
         x_last = ws.xs[c.num_hidden_layers] if train else ws.xs[c.num_hidden_layers % 2]
         self._norm_fwd(x_last, fl.p32_view("norm.weight", (c.hidden_size,)), self._bias_view(fl.p32_view, "norm.bias"),
                        ws.hf, ws.meanf, ws.rstdf)
-        ops.gemm_f16(ws.hf, e16, out=ws.logits)
+        if ce:  # the head also leaves the cross-entropy statistics of its logits (ce_fwd_parts)
+            ops.gemm_f16_ce_parts(ws.hf, e16, out=ws.logits, parts=ws.ce_parts)
+        else:
+            ops.gemm_f16(ws.hf, e16, out=ws.logits)
         ws.extra["x_last"] = x_last
         return ws
 
@@ -455,11 +460,12 @@ class JishuiForCausalLM(nn.Module):
         tg = targets.to(torch.int64).contiguous()
         if torch.is_grad_enabled() and self.embed_tokens.weight.requires_grad:
             return _LossFn.apply(self, ids, tg, ignore_index, *self.parameters())
-        ws = self._trunk_fwd(ids, train=False)
+        ws = self._trunk_fwd(ids, train=False, ce=True)
         return self._ce_forward(ws, tg.reshape(-1), ignore_index)[2].clone()
 
     def _ce_forward(self, ws: Workspace, tg: torch.Tensor, ignore_index: int) -> torch.Tensor:
-        ops.ce_fwd(ws.logits, tg, ignore_index, lse=ws.ce_lse, row_loss=ws.row_loss)
+        """Loss from the statistics the head left in ws.ce_parts (the trunk ran with ce=True)."""
+        ops.ce_fwd_parts(ws.ce_parts, ws.logits, tg, ignore_index, lse=ws.ce_lse, row_loss=ws.row_loss)
         out = torch.empty(3, dtype=torch.float32, device=ws.logits.device)
         ops.ce_loss(ws.row_loss, tg, ignore_index, out=out)
         return out
@@ -525,7 +531,7 @@ class _LossFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, model: JishuiForCausalLM, ids, targets, ignore_index, *params):
-        ws = model._trunk_fwd(ids, train=True)
+        ws = model._trunk_fwd(ids, train=True, ce=True)
         tg = targets.reshape(-1)
         out = model._ce_forward(ws, tg, ignore_index)
         model._gen += 1

@@ -339,6 +339,47 @@ def ce_fwd(logits16: torch.Tensor, targets: torch.Tensor, ignore_index: int = -1
     return lse, row_loss
 
 
+def ce_parts_blocks(vocab: int) -> int:
+    """Number of 128-column blocks of the head's cross-entropy partial statistics."""
+    return (vocab + 127) // 128
+
+
+def gemm_f16_ce_parts(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+                      parts: torch.Tensor | None = None):
+    """The tied head C = a b^T (fp16 logits, as gemm_f16) plus parts [M, ceil(N/128), 2] fp32: (max,
+    sum exp(v - max)) of each 128-column block of the fp16 logits v, for ce_fwd_parts."""
+    _check(a, F16, "a", contiguous=False)
+    _check(b, F16, "b", contiguous=False)
+    M, K = a.shape
+    N, Kb = b.shape
+    if K != Kb:
+        raise ValueError(f"inner dimensions differ: {K} vs {Kb}")
+    c = out if out is not None else torch.empty(M, N, device=a.device, dtype=F16)
+    nblk = ce_parts_blocks(N)
+    if parts is None:
+        parts = torch.empty(M, nblk, 2, device=a.device, dtype=F32)
+    _check(parts, F32, "parts")
+    if parts.numel() < M * nblk * 2:
+        raise ValueError("parts is too small")
+    with _GemmTimer(2.0 * M * N * K, 2.0 * (M * K + N * K + M * N)):
+        _lib.call("jx_gemm_f16_ce_parts", a.data_ptr(), _ld(a), b.data_ptr(), _ld(b), M, N, K, c.data_ptr(), _ld(c),
+                  parts.data_ptr(), _stream())
+    return c, parts
+
+
+def ce_fwd_parts(parts: torch.Tensor, logits16: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100,
+                 lse=None, row_loss=None):
+    """ce_fwd from the head GEMM's partial statistics (only the target logits are read)."""
+    _check(targets, I64, "targets")
+    _check(parts, F32, "parts")
+    rows, vocab = logits16.shape
+    lse = lse if lse is not None else torch.empty(rows, device=logits16.device, dtype=F32)
+    row_loss = row_loss if row_loss is not None else torch.empty(rows, device=logits16.device, dtype=F32)
+    _lib.call("jx_ce_fwd_parts", parts.data_ptr(), ce_parts_blocks(vocab), logits16.data_ptr(), rows, vocab,
+              _ld(logits16), targets.data_ptr(), ignore_index, lse.data_ptr(), row_loss.data_ptr(), _stream())
+    return lse, row_loss
+
+
 def ce_loss(row_loss: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100,
             out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
     out = out if out is not None else torch.zeros(3, device=row_loss.device, dtype=F32)

@@ -156,6 +156,24 @@ def test_gemm_qkv_rope_table_paths(ops, gemm_mode):
         ops.gemm_qkv_rope(x, w, d, buf[1:].view(T + 1, hd // 2), sin, T + 1, hd)
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 1000, 256), (1024, 32000, 1024), (64, 2056, 128)])
+def test_head_ce_parts(ops, gemm_mode, M, N, K):
+    """The tied head with the cross-entropy statistics in its epilogue: its logits equal gemm_f16's bit for
+    bit, and lse / loss merged from the per-block statistics match ce_fwd over the stored logits and torch's
+    logsumexp (row tiles past M, a last 128-column block past N)."""
+    a, b = _h(M, K, seed=50), _h(N, K, scale=0.5, seed=51)
+    logits, parts = ops.gemm_f16_ce_parts(a, b)
+    assert torch.equal(logits, ops.gemm_f16(a, b))
+    g = torch.Generator(device="cuda").manual_seed(52)
+    tg = torch.randint(0, N, (M,), device="cuda", generator=g)
+    tg[::7] = -100
+    lse_ref, loss_ref = ops.ce_fwd(logits, tg)
+    lse, loss = ops.ce_fwd_parts(parts, logits, tg)
+    assert torch.allclose(lse, lse_ref, rtol=1e-6, atol=1e-5)
+    assert torch.allclose(loss, loss_ref, rtol=1e-5, atol=1e-5)
+    assert torch.allclose(lse, torch.logsumexp(logits.float(), dim=1), rtol=1e-6, atol=1e-5)
+
+
 def test_swiglu_fwd_bwd(ops, gemm_mode):
     M, d, F = 512, 256, 688
     x = _h(M, d, seed=6)
