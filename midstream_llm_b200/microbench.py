@@ -99,9 +99,11 @@ def bench_ce(iters: int) -> None:
     dE = torch.zeros(V, d, device="cuda")
     grad = torch.tensor([65536.0 / 4], device="cuda")
 
-    def step():
-        ops.gemm_f16(h, E, out=logits)
-        ops.ce_fwd(logits, tg, lse=lse, row_loss=row_loss)
+    parts = torch.empty(M, ops.ce_parts_blocks(V), 2, device="cuda")
+
+    def step():  # the model's path: head GEMM with the CE statistics in its epilogue
+        ops.gemm_f16_ce_parts(h, E, out=logits, parts=parts)
+        ops.ce_fwd_parts(parts, logits, tg, lse=lse, row_loss=row_loss)
         ops.ce_loss(row_loss, tg, out=lsc)
         ops.ce_bwd(logits, tg, lse, grad, lsc[1:2])
         ops.gemm_f16(logits, E, b_mn_major=True, out=dh)
@@ -110,10 +112,15 @@ def bench_ce(iters: int) -> None:
     t = _time(step, iters)
     _emit("fused_ce fwd+bwd h[16384,1024] x E[32000,1024]", t, 3 * 2.0 * M * V * d, "TFLOP/s",
           pk.get("bf16_tflops_sustained", pk["bf16_tflops"]), flops=3 * 2.0 * M * V * d)
-    t_fwd = _time(lambda: ops.ce_fwd(logits, tg, lse=lse, row_loss=row_loss), iters)
+    # The bandwidth-bound softmax sub-steps: the statistics merge (parts + target logits) and the backward
+    # read / write of the fp16 logits; the unfused form reads the logits once more in the forward.
+    t_fwd = _time(lambda: ops.ce_fwd_parts(parts, logits, tg, lse=lse, row_loss=row_loss), iters)
     t_bwd = _time(lambda: ops.ce_bwd(logits, tg, lse, grad, lsc[1:2]), iters)
-    _emit("ce_softmax_substeps (fwd read + bwd read/write of fp16 logits)", t_fwd + t_bwd, 3 * M * V * 2, "GB/s",
-          pk["hbm_gbs"], fwd_us=t_fwd * 1e6, bwd_us=t_bwd * 1e6, unfused_bytes=2 * M * V * 2)
+    t_unf = _time(lambda: ops.ce_fwd(logits, tg, lse=lse, row_loss=row_loss), iters)
+    moved = parts.numel() * 4 + 2 * M * V * 2
+    _emit("ce_softmax_substeps (statistics merge + bwd read/write of fp16 logits)", t_fwd + t_bwd, moved, "GB/s",
+          pk["hbm_gbs"], fwd_us=t_fwd * 1e6, bwd_us=t_bwd * 1e6, unfused_fwd_us=t_unf * 1e6,
+          unfused_bytes=3 * M * V * 2)
 
 
 def bench_adamw(iters: int) -> None:
