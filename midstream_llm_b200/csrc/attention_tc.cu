@@ -617,7 +617,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t dSt = smem_desc_sw128(smem_u32(sSt), 16384, 1024); // MN-major A of dQ (buffer 0)
       // S^T / dP^T of query half hf of ring tile g with K / V buffer kvb: M 128 keys, N 64
       // queries, into TMEM columns [64 hf, 64 hf + 64) and [128 + 64 hf, ...).
-      auto issue_sdp = [&](uint32_t g, int hf, int kvb) {
+      auto issue_sdp = [&](uint32_t g, auto hc, int kvb) {
+        constexpr int hf = decltype(hc)::value;
         const uint32_t off = (g & 1) * kTileBytes + hf * 8192;
         const uint32_t kvo = kvb * 2 * kTileBytes;
         const uint64_t bq = desc_adv(dQk, off), bo = desc_adv(dOk, off);
@@ -637,8 +638,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
              wait(&bars->q_full[0], 0, abort_flag, status, kFaMma);
         if (ok) {
           tc_fence_after();
-          issue_sdp(0, 0, 0);
-          issue_sdp(0, 1, 0);
+          issue_sdp(0, std::integral_constant<int, 0>{}, 0);
+          issue_sdp(0, std::integral_constant<int, 1>{}, 0);
         }
       }
       for (uint32_t n = 0; ok && idx >= 0 && idx < total; ++n) {
@@ -650,13 +651,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int t = 0; t < ntiles && ok; ++t, ++g) {
           const int s = g & 1;
           const uint64_t bq = desc_adv(dQmn, s * kTileBytes), bo = desc_adv(dOmn, s * kTileBytes);
-          for (int hf = 0; hf < 2 && ok; ++hf) {
+          // The half index is a compile-time constant in each copy of the body (TMEM columns, descriptor
+          // offsets and barrier addresses fold into immediates).
+          auto half = [&](auto hc) {
+            constexpr int hf = decltype(hc)::value;
             // P^T / dS^T of this half are in TMEM (over its S^T / dP^T columns).
-            if (!(ok = wait(&bars->p_full[hf], g & 1, abort_flag, status, kFaMma))) break;
+            if (!(ok = wait(&bars->p_full[hf], g & 1, abort_flag, status, kFaMma))) return;
             // The first dV / dK products of an item overwrite the accumulators: the previous
             // item's epilogue has read them.
             if (t == 0 && hf == 0 && n > 0 && !(ok = wait(&bars->acc_drained, (n - 1) & 1, abort_flag, status, kFaMma)))
-              break;
+              return;
             tc_fence_after();
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -670,27 +674,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             // tensor core runs a thread's products in issue order.
             if (t + 1 < ntiles) {
               if (hf == 0) {
-                if (!(ok = wait(&bars->q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma))) break;
+                if (!(ok = wait(&bars->q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma))) return;
                 tc_fence_after();
               }
-              issue_sdp(g + 1, hf, kvb);
+              issue_sdp(g + 1, hc, kvb);
             } else {
               if (hf == 0) {
                 next = ring_take(&bars->items, n + 1, abort_flag, status, kFaMma);
                 if (next < 0) {
                   ok = false;
-                  break;
+                  return;
                 }
                 if (next < total) {
                   if (!(ok = wait(&bars->kv_full[kvb ^ 1], ((n + 1) >> 1) & 1, abort_flag, status, kFaMma) &&
                              wait(&bars->q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma)))
-                    break;
+                    return;
                   tc_fence_after();
                 }
               }
-              if (next < total) issue_sdp(g + 1, hf, kvb ^ 1);  // the next item's first tile
+              if (next < total) issue_sdp(g + 1, hc, kvb ^ 1);  // the next item's first tile
             }
-          }
+          };
+          half(std::integral_constant<int, 0>{});
+          if (ok) half(std::integral_constant<int, 1>{});
           if (!ok) break;
           if (!(ok = wait(&bars->dq_free[g & 1], ((g >> 1) & 1) ^ 1, abort_flag, status, kFaMma))) break;
           tc_fence_after();
