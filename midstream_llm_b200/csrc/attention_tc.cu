@@ -617,9 +617,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t dSt = smem_desc_sw128(smem_u32(sSt), 16384, 1024); // MN-major A of dQ (buffer 0)
       // S^T / dP^T of query half hf of ring tile g with K / V buffer kvb: M 128 keys, N 64
       // queries, into TMEM columns [64 hf, 64 hf + 64) and [128 + 64 hf, ...).
-      auto issue_sdp = [&](uint32_t g, auto hc, int kvb) {
+      auto issue_sdp = [&](uint32_t g, auto hc, auto slot_c, int kvb) {
         constexpr int hf = decltype(hc)::value;
-        const uint32_t off = (g & 1) * kTileBytes + hf * 8192;
+        constexpr int SL = decltype(slot_c)::value;  // ring slot of tile g (g & 1)
+        (void)g;
+        const uint32_t off = SL * kTileBytes + hf * 8192;
         const uint32_t kvo = kvb * 2 * kTileBytes;
         const uint64_t bq = desc_adv(dQk, off), bo = desc_adv(dOk, off);
         const uint64_t ak = desc_adv(dK, kvo), av = desc_adv(dV, kvo);
@@ -638,8 +640,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
              wait(&bars->q_full[0], 0, abort_flag, status, kFaMma);
         if (ok) {
           tc_fence_after();
-          issue_sdp(0, std::integral_constant<int, 0>{}, 0);
-          issue_sdp(0, std::integral_constant<int, 1>{}, 0);
+          issue_sdp(0, std::integral_constant<int, 0>{}, std::integral_constant<int, 0>{}, 0);
+          issue_sdp(0, std::integral_constant<int, 1>{}, std::integral_constant<int, 0>{}, 0);
         }
       }
       for (uint32_t n = 0; ok && idx >= 0 && idx < total; ++n) {
@@ -649,66 +651,73 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint64_t kmn = desc_adv(dKmn, kvb * 2 * kTileBytes);
         int next = -1;  // the following item, taken during this item's last tile
         for (int t = 0; t < ntiles && ok; ++t, ++g) {
-          const int s = g & 1;
-          const uint64_t bq = desc_adv(dQmn, s * kTileBytes), bo = desc_adv(dOmn, s * kTileBytes);
-          // The half index is a compile-time constant in each copy of the body (TMEM columns, descriptor
-          // offsets and barrier addresses fold into immediates).
-          auto half = [&](auto hc) {
-            constexpr int hf = decltype(hc)::value;
-            // P^T / dS^T of this half are in TMEM (over its S^T / dP^T columns).
-            if (!(ok = wait(&bars->p_full[hf], g & 1, abort_flag, status, kFaMma))) return;
-            // The first dV / dK products of an item overwrite the accumulators: the previous
-            // item's epilogue has read them.
-            if (t == 0 && hf == 0 && n > 0 && !(ok = wait(&bars->acc_drained, (n - 1) & 1, abort_flag, status, kFaMma)))
-              return;
-            tc_fence_after();
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int kk = hf * 4 + j;  // 16 queries per step
-              const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-              umma_f16_ts(tmem + 256, tmem + pair_col(kk), desc_adv(bo, kk * 2048), id_kn, acc);
-              umma_f16_ts(tmem + 320, tmem + 128 + pair_col(kk), desc_adv(bq, kk * 2048), id_kn, acc);
-            }
-            if (hf == 1) umma_commit(&bars->q_empty[s]);  // Q / dO / LSE / Delta of this slot are no longer read
-            // The next tile's scores of this half overwrite the columns dV / dK just read; the
-            // tensor core runs a thread's products in issue order.
-            if (t + 1 < ntiles) {
-              if (hf == 0) {
-                if (!(ok = wait(&bars->q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma))) return;
-                tc_fence_after();
+          // The ring slot (g & 1) is a compile-time constant in each copy of the tile body.
+          auto tile = [&](auto sc) {
+            constexpr int S = decltype(sc)::value;
+            const uint64_t bq = desc_adv(dQmn, S * kTileBytes), bo = desc_adv(dOmn, S * kTileBytes);
+            // The half index is a compile-time constant in each copy of the body (TMEM columns, descriptor
+            // offsets and barrier addresses fold into immediates).
+            auto half = [&](auto hc) {
+              constexpr int hf = decltype(hc)::value;
+              // P^T / dS^T of this half are in TMEM (over its S^T / dP^T columns).
+              if (!(ok = wait(&bars->p_full[hf], S, abort_flag, status, kFaMma))) return;
+              // The first dV / dK products of an item overwrite the accumulators: the previous
+              // item's epilogue has read them.
+              if (t == 0 && hf == 0 && n > 0 && !(ok = wait(&bars->acc_drained, (n - 1) & 1, abort_flag, status, kFaMma)))
+                return;
+              tc_fence_after();
+  #pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int kk = hf * 4 + j;  // 16 queries per step
+                const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+                umma_f16_ts(tmem + 256, tmem + pair_col(kk), desc_adv(bo, kk * 2048), id_kn, acc);
+                umma_f16_ts(tmem + 320, tmem + 128 + pair_col(kk), desc_adv(bq, kk * 2048), id_kn, acc);
               }
-              issue_sdp(g + 1, hc, kvb);
-            } else {
-              if (hf == 0) {
-                next = ring_take(&bars->items, n + 1, abort_flag, status, kFaMma);
-                if (next < 0) {
-                  ok = false;
-                  return;
-                }
-                if (next < total) {
-                  if (!(ok = wait(&bars->kv_full[kvb ^ 1], ((n + 1) >> 1) & 1, abort_flag, status, kFaMma) &&
-                             wait(&bars->q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma)))
-                    return;
+              if (hf == 1) umma_commit(&bars->q_empty[S]);  // Q / dO / LSE / Delta of this slot are no longer read
+              // The next tile's scores of this half overwrite the columns dV / dK just read; the
+              // tensor core runs a thread's products in issue order.
+              if (t + 1 < ntiles) {
+                if (hf == 0) {
+                  if (!(ok = wait(&bars->q_full[1 - S], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma))) return;
                   tc_fence_after();
                 }
+                issue_sdp(g + 1, hc, std::integral_constant<int, 1 - S>{}, kvb);
+              } else {
+                if (hf == 0) {
+                  next = ring_take(&bars->items, n + 1, abort_flag, status, kFaMma);
+                  if (next < 0) {
+                    ok = false;
+                    return;
+                  }
+                  if (next < total) {
+                    if (!(ok = wait(&bars->kv_full[kvb ^ 1], ((n + 1) >> 1) & 1, abort_flag, status, kFaMma) &&
+                               wait(&bars->q_full[1 - S], ((g + 1) >> 1) & 1, abort_flag, status, kFaMma)))
+                      return;
+                    tc_fence_after();
+                  }
+                }
+                if (next < total) issue_sdp(g + 1, hc, std::integral_constant<int, 1 - S>{}, kvb ^ 1);  // next item's first tile
               }
-              if (next < total) issue_sdp(g + 1, hc, kvb ^ 1);  // the next item's first tile
+            };
+            half(std::integral_constant<int, 0>{});
+            if (ok) half(std::integral_constant<int, 1>{});
+            if (!ok) return;
+            if (!(ok = wait(&bars->dq_free[S], ((g >> 1) & 1) ^ 1, abort_flag, status, kFaMma))) return;
+            tc_fence_after();
+            const uint64_t sbuf = desc_adv(dSt, S * kPBytes);
+  #pragma unroll
+            for (int kk = 0; kk < BKV / 16; ++kk) {
+              // dS^T read MN-major: queries contiguous (two 64-query halves 16 KiB apart), 16 keys per step.
+              umma_f16(tmem + 384 + S * D, desc_adv(sbuf, kk * 2048), desc_adv(kmn, kk * 2048), id_q,
+                       kk > 0 ? 1u : 0u);
             }
+            umma_commit(&bars->grads_done);
+            if (t + 1 == ntiles) umma_commit(&bars->kv_empty[kvb]);  // K / V of this item are no longer read
           };
-          half(std::integral_constant<int, 0>{});
-          if (ok) half(std::integral_constant<int, 1>{});
-          if (!ok) break;
-          if (!(ok = wait(&bars->dq_free[g & 1], ((g >> 1) & 1) ^ 1, abort_flag, status, kFaMma))) break;
-          tc_fence_after();
-          const uint64_t sbuf = desc_adv(dSt, s * kPBytes);
-#pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            // dS^T read MN-major: queries contiguous (two 64-query halves 16 KiB apart), 16 keys per step.
-            umma_f16(tmem + 384 + (g & 1) * D, desc_adv(sbuf, kk * 2048), desc_adv(kmn, kk * 2048), id_q,
-                     kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&bars->grads_done);
-          if (t + 1 == ntiles) umma_commit(&bars->kv_empty[kvb]);  // K / V of this item are no longer read
+          if (g & 1)
+            tile(std::integral_constant<int, 1>{});
+          else
+            tile(std::integral_constant<int, 0>{});
         }
         idx = next;
       }
