@@ -96,7 +96,9 @@ int jx_layernorm_bwd(const void* dy, const void* x, const float* mean, const flo
  * on every GPU that loads it until the process exits; cols above 1024 are
  * rejected with JX_ERR_INVALID. The first call on a device looks up that
  * array's device address (cudaGetSymbolAddress with the device current), so
- * make a first call on each device before any stream capture. All calls share
+ * make a first call on each device before any stream capture. The looked-up
+ * address is cached per device and keyed on the CUDA context, so after a
+ * device reset (cudaDeviceReset) the next call looks it up again. All calls share
  * the one array: calls that overlap on the GPU (e.g. on two streams at once)
  * race; nothing from an earlier call is read, so no clearing is needed.
  * This entry point has no counterpart in the reference project. */
@@ -147,7 +149,9 @@ int64_t jx_gemm_wgrad_workspace_bytes(int N, int K, int splits);
 /* Kernel choice for all GEMM entry points: 0 (default) runs the 2-SM
  * kernel (a CTA pair per 256 x 256 tile, tcgen05 cta_group::2) whenever M
  * spans at least two 128-row blocks and the 1-SM kernel otherwise; 1 forces
- * the 1-SM kernel, 2 the 2-SM kernel. Process-wide; results are identical. */
+ * the 1-SM kernel, 2 the 2-SM kernel. A test / diagnostic switch: it is kept
+ * per host thread (it affects only calls made from the thread that set it),
+ * and both kernels give identical results. */
 int jx_gemm_set_mode(int mode);
 int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_t ldx, int T, int N, int K, float* G,
                   int64_t ldg, int accumulate, int splits, void* workspace, jx_stream_t stream);
@@ -194,7 +198,10 @@ int jx_pack_rows(const void* tokens, int64_t ntokens, const int64_t* runs, const
 
 /* ---- Cross-entropy over f16 logits (model_torch.py:102-104) ----
  * Per row: lse = log(sum exp(logit)), loss = lse - logit[target]; rows whose
- * target == ignore_index give loss 0 and are excluded from the mean. */
+ * target == ignore_index give loss 0 and are excluded from the mean. A target
+ * outside [0, vocab) that is not ignore_index (torch rejects it) gives a NaN
+ * row loss, so the mean is NaN, and sets the device status word to 202
+ * (jx_device_status); jx_ce_bwd gives such a row a zero gradient. */
 int jx_ce_fwd(const void* logits16, int64_t rows, int vocab, int64_t ld, const int64_t* targets, int64_t ignore_index,
               float* lse, float* row_loss, jx_stream_t stream);
 /* The tied head with the cross-entropy statistics in its epilogue: C = A B^T as jx_gemm_f16 (A [M, K],

@@ -1,18 +1,56 @@
-"""Run configuration: the same dataclasses, fields, defaults and validation as
-the reference (Midstream-LLM src/jishui/config.py:11-112), so JSON run configs
-and checkpoint `train_state.json` records load unchanged."""
+"""Run configuration records for the Jishui decoder and its trainer.
+
+The field names, their order and their defaults are an interface shared with
+Midstream-LLM (src/jishui/config.py:11-99): run-config JSON files
+(`{"model": {...}, "training": {...}}`) and the `model` record stored in every
+checkpoint's `train_state.json` are written by one trainer and read by the
+other, so both records round-trip through `to_dict()` / `from_dict()`
+unchanged. The checks below are derived from what each field means to the
+model and the update loop; each record reports every violated constraint at
+once in a single ValueError.
+
+`JishuiForCausalLM` accepts any object carrying these attributes, including the
+reference's own `ModelConfig`.
+"""
 from __future__ import annotations
 
 import json
 import math
 from dataclasses import asdict, dataclass
 from pathlib import Path
-from typing import Any
+from typing import Any, Iterator
+
+NORM_TYPES = ("layernorm", "rmsnorm")
+COMPUTE_DTYPES = ("float32", "float16", "bfloat16")
+SAMPLING_MODES = ("target", "weights")
+
+
+class _Record:
+    """JSON round-trip shared by both records: unknown keys are an error (TypeError from the constructor)."""
+
+    @classmethod
+    def from_dict(cls, value: dict[str, Any]):
+        return cls(**value)
+
+    @classmethod
+    def from_json(cls, path: str | Path):
+        return cls.from_dict(json.loads(Path(path).read_text(encoding="utf-8")))
+
+    def to_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+    def _violations(self) -> Iterator[str]:  # pragma: no cover - overridden
+        return iter(())
+
+    def __post_init__(self) -> None:
+        problems = list(self._violations())
+        if problems:
+            raise ValueError(f"invalid {type(self).__name__}: " + "; ".join(problems))
 
 
 @dataclass(frozen=True)
-class ModelConfig:
-    """Decoder architecture (config.py:11-41). Validation matches the reference."""
+class ModelConfig(_Record):
+    """Decoder architecture (the reference's config.py:11-28 fields)."""
     name: str
     vocab_size: int
     hidden_size: int
@@ -31,34 +69,24 @@ class ModelConfig:
     mlp_bias: bool = False
     gradient_checkpointing: bool = True
 
-    def __post_init__(self) -> None:
-        if self.hidden_size != self.num_attention_heads * self.head_dim:
-            raise ValueError(
-                "hidden_size must equal num_attention_heads * head_dim: "
-                f"{self.hidden_size} != {self.num_attention_heads} * {self.head_dim}")
-        if self.num_attention_heads % self.num_key_value_heads != 0:
-            raise ValueError("num_attention_heads must be divisible by num_key_value_heads")
+    def _violations(self) -> Iterator[str]:
+        # The attention heads tile the hidden state exactly.
+        if self.num_attention_heads * self.head_dim != self.hidden_size:
+            yield (f"hidden_size must equal num_attention_heads * head_dim ({self.hidden_size} != "
+                   f"{self.num_attention_heads} * {self.head_dim})")
+        # Each key/value head serves a whole group of query heads.
+        if self.num_key_value_heads < 1 or self.num_attention_heads % self.num_key_value_heads:
+            yield "num_attention_heads must be divisible by num_key_value_heads"
+        # RoPE rotates the two halves of every head against each other.
         if self.head_dim % 2:
-            raise ValueError("head_dim must be even for RoPE")
-        if self.norm_type not in {"layernorm", "rmsnorm"}:
-            raise ValueError("norm_type must be layernorm or rmsnorm")
-
-    @classmethod
-    def from_dict(cls, value: dict[str, Any]) -> "ModelConfig":
-        return cls(**value)
-
-    @classmethod
-    def from_json(cls, path: str | Path) -> "ModelConfig":
-        with Path(path).open(encoding="utf-8") as handle:
-            return cls.from_dict(json.load(handle))
-
-    def to_dict(self) -> dict[str, Any]:
-        return asdict(self)
+            yield "head_dim must be even for RoPE"
+        if self.norm_type not in NORM_TYPES:
+            yield f"norm_type must be one of {', '.join(NORM_TYPES)} (got {self.norm_type!r})"
 
 
 @dataclass(frozen=True)
-class TrainConfig:
-    """Optimizer / AMP / loop inputs (config.py:57-99)."""
+class TrainConfig(_Record):
+    """Optimizer, AMP and loop inputs (the reference's config.py:57-83 fields)."""
     seed: int = 42
     dtype: str = "float16"
     loss_scale: float = 1.0
@@ -84,34 +112,32 @@ class TrainConfig:
     eod_token_id: int = 2
     compile_step: bool = True
 
-    def __post_init__(self) -> None:
-        if self.dtype not in {"float32", "float16", "bfloat16"}:
-            raise ValueError("dtype must be float32, float16, or bfloat16")
-        if not math.isfinite(self.loss_scale) or self.loss_scale <= 0:
-            raise ValueError("loss_scale must be finite and positive")
-        if min(self.seq_len, self.batch_size, self.grad_accum_steps, self.max_steps) < 1:
-            raise ValueError("sequence, batch, accumulation, and step values must be positive")
-        if self.sampling_mode not in {"target", "weights"}:
-            raise ValueError("sampling_mode must be target or weights")
-        if self.adam_eps <= 0:
-            raise ValueError("adam_eps must be positive")
+    def _violations(self) -> Iterator[str]:
+        if self.dtype not in COMPUTE_DTYPES:
+            yield f"dtype must be one of {', '.join(COMPUTE_DTYPES)} (got {self.dtype!r})"
+        # The initial GradScaler scale multiplies the loss.
+        if not (math.isfinite(self.loss_scale) and self.loss_scale > 0):
+            yield "loss_scale must be finite and positive"
+        sizes = {"seq_len": self.seq_len, "batch_size": self.batch_size,
+                 "grad_accum_steps": self.grad_accum_steps, "max_steps": self.max_steps}
+        for key, value in sizes.items():
+            if value < 1:
+                yield f"{key} must be positive (got {value})"
+        if self.sampling_mode not in SAMPLING_MODES:
+            yield f"sampling_mode must be one of {', '.join(SAMPLING_MODES)} (got {self.sampling_mode!r})"
+        # AdamW divides by sqrt(v) + eps.
+        if not self.adam_eps > 0:
+            yield "adam_eps must be positive"
         if self.max_checkpoints < 1:
-            raise ValueError("max_checkpoints must be positive")
-        if self.optimizer_checkpoints < 0 or self.optimizer_checkpoints > self.max_checkpoints:
-            raise ValueError("optimizer_checkpoints must be between 0 and max_checkpoints")
-
-    @classmethod
-    def from_dict(cls, value: dict[str, Any]) -> "TrainConfig":
-        return cls(**value)
-
-    def to_dict(self) -> dict[str, Any]:
-        return asdict(self)
+            yield "max_checkpoints must be positive"
+        # Optimizer state is kept in a subset of the retained checkpoints.
+        if not 0 <= self.optimizer_checkpoints <= self.max_checkpoints:
+            yield "optimizer_checkpoints must be between 0 and max_checkpoints"
 
 
 def load_run_config(path: str | Path) -> tuple[ModelConfig, TrainConfig]:
-    """Reads the {model, training, ...} JSON run config (config.py:109-112)."""
-    with Path(path).open(encoding="utf-8") as handle:
-        raw = json.load(handle)
+    """Both records of a `{"model": ..., "training": ...}` run-config file."""
+    raw = json.loads(Path(path).read_text(encoding="utf-8"))
     return ModelConfig.from_dict(raw["model"]), TrainConfig.from_dict(raw["training"])
 
 

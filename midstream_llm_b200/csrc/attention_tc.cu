@@ -949,12 +949,12 @@ extern "C" int jx_attn_fwd(const void* qkv, void* out, float* lse, void* workspa
   const int64_t cols = 3LL * H * D;
   CUtensorMap tm;
   JX_CHECK_ARG(make_tmap_f16(&tm, qkv, cols, rows, cols, D, BKV), "jx_attn_fwd: cannot encode TMA descriptor");
-  static bool attr_set = false;
-  if (!attr_set) {
-    JX_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes),
-                "jx_attn_fwd: smem attribute");
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};
+  JX_CUDA_TRY(once_per_device(attr_set, [] {
+                return cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)kSmemBytes);
+              }),
+              "jx_attn_fwd: smem attribute");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int* counter = static_cast<int*>(workspace);
   JX_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int), s), "jx_attn_fwd: clear work counter");
@@ -1009,12 +1009,12 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
               "jx_attn_bwd: clear dq accumulator");
   jx::attn::launch_delta(static_cast<const __half*>(out), static_cast<const __half*>(dout), lse, delta, nl2, B, T, H, s);
   JX_CHECK_LAUNCH("jx_attn_bwd: delta");
-  static bool attr_set = false;
-  if (!attr_set) {
-    JX_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem),
-                "jx_attn_bwd: smem attribute");
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};
+  JX_CUDA_TRY(once_per_device(attr_set, [] {
+                return cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)kBwdSmem);
+              }),
+              "jx_attn_bwd: smem attribute");
   const int64_t items = (int64_t)(T / BQ) * H * B;
   const int grid = (int)std::min<int64_t>(items, num_sms());
   attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, tdq, nl2, delta, dq_acc, static_cast<__half*>(dqkv),

@@ -49,10 +49,26 @@ __global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, int64_t ntok, 
   }
 }
 
+// Loss of one row from its log-sum-exp and target. A target outside [0, vocab) that is not ignore_index
+// (torch's cross_entropy rejects it) gives a NaN loss, so the mean loss is NaN and the trainer refuses the
+// update, and records kStatusCeBadTarget in the device status word; the backward gives such a row no
+// gradient (ce_target_valid).
+__device__ __forceinline__ bool ce_target_valid(int64_t t, int vocab) { return t >= 0 && t < vocab; }
+
+__device__ __forceinline__ float target_loss(int64_t t, int64_t ignore_index, int vocab, float lse_row,
+                                             const __half* row_logits, int* status) {
+  if (t == ignore_index) return 0.f;
+  if (!ce_target_valid(t, vocab)) {
+    if (status) atomicExch(status, kStatusCeBadTarget);
+    return __int_as_float(0x7fc00000);
+  }
+  return lse_row - __half2float(row_logits[t]);
+}
+
 // One warp per row: online max / sum-of-exp over the row with 16-byte loads.
 __global__ void ce_fwd_kernel(const __half* __restrict__ logits, int64_t rows, int vocab, int64_t ld,
                               const int64_t* __restrict__ targets, int64_t ignore_index, float* __restrict__ lse,
-                              float* __restrict__ row_loss) {
+                              float* __restrict__ row_loss, int* status) {
   const int lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -93,13 +109,7 @@ __global__ void ce_fwd_kernel(const __half* __restrict__ logits, int64_t rows, i
   if (lane == 0) {
     const float l = gm + logf(s);
     lse[row] = l;
-    const int64_t t = targets[row];
-    float loss = 0.f;
-    if (t != ignore_index) {
-      const int64_t tc = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
-      loss = l - __half2float(x[tc]);
-    }
-    row_loss[row] = loss;
+    row_loss[row] = target_loss(targets[row], ignore_index, vocab, l, x, status);
   }
 }
 
@@ -108,7 +118,8 @@ __global__ void ce_fwd_kernel(const __half* __restrict__ logits, int64_t rows, i
 // (lse = M + log sum_b s_b exp(m_b - M)) and reads the target's logit, so the logits are not read again.
 __global__ void ce_fwd_parts_kernel(const float2* __restrict__ parts, int nblk, const __half* __restrict__ logits,
                                     int64_t rows, int vocab, int64_t ld, const int64_t* __restrict__ targets,
-                                    int64_t ignore_index, float* __restrict__ lse, float* __restrict__ row_loss) {
+                                    int64_t ignore_index, float* __restrict__ lse, float* __restrict__ row_loss,
+                                    int* status) {
   const int lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -127,13 +138,7 @@ __global__ void ce_fwd_parts_kernel(const float2* __restrict__ parts, int nblk, 
   if (lane == 0) {
     const float l = gm + logf(s);
     lse[row] = l;
-    const int64_t t = targets[row];
-    float loss = 0.f;
-    if (t != ignore_index) {
-      const int64_t tc = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
-      loss = l - __half2float(logits[row * ld + tc]);
-    }
-    row_loss[row] = loss;
+    row_loss[row] = target_loss(targets[row], ignore_index, vocab, l, logits + row * ld, status);
   }
 }
 
@@ -179,7 +184,7 @@ __global__ void ce_bwd_kernel(__half* __restrict__ logits, int64_t rows, int voc
   __half* x = logits + row * ld;
   const int64_t t = targets[row];
   const float cnt = *count;
-  const float g = (t == ignore_index || cnt <= 0.f) ? 0.f : (*grad_loss) / cnt;
+  const float g = (t == ignore_index || !ce_target_valid(t, vocab) || cnt <= 0.f) ? 0.f : (*grad_loss) / cnt;
   const float l = lse[row];
   const int nvec = vocab / 8;
   for (int i = lane; i < nvec; i += 32) {
@@ -236,7 +241,7 @@ extern "C" int jx_ce_fwd(const void* logits16, int64_t rows, int vocab, int64_t 
   JX_CHECK_ARG(ld % 8 == 0 && aligned16(logits16), "jx_ce_fwd: ld%%8 and 16B alignment required");
   const unsigned grid = (unsigned)((rows + kWarps - 1) / kWarps);
   ce_fwd_kernel<<<grid, kWarps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(logits16), rows, vocab, ld, targets, ignore_index, lse, row_loss);
+      static_cast<const __half*>(logits16), rows, vocab, ld, targets, ignore_index, lse, row_loss, status_ptr());
   JX_CHECK_LAUNCH("jx_ce_fwd");
   return JX_OK;
 }
@@ -250,7 +255,7 @@ extern "C" int jx_ce_fwd_parts(const void* parts, int nblk, const void* logits16
   const unsigned grid = (unsigned)((rows + kWarps - 1) / kWarps);
   ce_fwd_parts_kernel<<<grid, kWarps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const float2*>(parts), nblk, static_cast<const __half*>(logits16), rows, vocab, ld, targets,
-      ignore_index, lse, row_loss);
+      ignore_index, lse, row_loss, status_ptr());
   JX_CHECK_LAUNCH("jx_ce_fwd_parts");
   return JX_OK;
 }

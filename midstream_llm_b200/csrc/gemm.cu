@@ -1200,7 +1200,8 @@ bool make_tmap_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
 namespace gemm {
 
 // 0: choose (2-SM when there are at least two 128-row blocks), 1: force 1-SM, 2: force 2-SM.
-static int g_gemm_mode = 0;
+// A test / diagnostic switch, kept per host thread (jx_gemm_set_mode).
+static thread_local int g_gemm_mode = 0;
 
 template <int EPI, bool A_MN, bool B_MN>
 static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params p, cudaStream_t stream,
@@ -1265,41 +1266,45 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
   p.status = status_ptr();
 
   if (two_sm) {
-    static int max_clusters = 0;  // per template instantiation
+    // Resident clusters per device, per template instantiation (0 = not measured yet).
+    static std::atomic<int> max_clusters[64];
+    int dev = 0;
+    JX_CUDA_TRY(cudaGetDevice(&dev), name);
+    std::atomic<int>& slot = max_clusters[dev & 63];
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem2_bytes<EPI>();
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (!max_clusters) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    if (slot.load(std::memory_order_acquire) == 0) {
       JX_CUDA_TRY(cudaFuncSetAttribute(gemm2_kernel<EPI, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem2_bytes<EPI>()),
                   name);
       cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
       int n = 0;
       JX_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, gemm2_kernel<EPI, A_MN, B_MN>, &cfg), name);
-      max_clusters = n > 0 ? n : 1;
+      slot.store(n > 0 ? n : 1, std::memory_order_release);
     }
+    const int max_cl = slot.load(std::memory_order_acquire);
     const int tiles2 = ((p.tiles_m + 1) / 2) * p.tiles_n * p.splits;
-    const int clusters = tiles2 < max_clusters ? tiles2 : max_clusters;
+    const int clusters = tiles2 < max_cl ? tiles2 : max_cl;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     JX_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm2_kernel<EPI, A_MN, B_MN>, ta, tb, tc0, tc1, tc2, tx0, tx1, p), name);
     JX_CHECK_LAUNCH(name);
     return JX_OK;
   }
-  static bool attr_set = false;  // per template instantiation
-  if (!attr_set) {
-    JX_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<EPI, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kSmemBytes),
-                name);
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};  // per template instantiation
+  JX_CUDA_TRY(once_per_device(attr_set, [] {
+                return cudaFuncSetAttribute(gemm_kernel<EPI, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)kSmemBytes);
+              }),
+              name);
   const int tiles = p.tiles_m * p.tiles_n * p.splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   gemm_kernel<EPI, A_MN, B_MN><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tc0, tc1, tc2, p);

@@ -28,20 +28,54 @@ void set_error(const char* fmt, ...) {
 static __device__ int g_device_status;
 
 static std::mutex g_mu;
-static int* g_status_ptr[64];
 static int g_sms[64];
 
-int* status_ptr() {
+// Driver calls reached through the runtime's entry-point query (the library does not link libcuda).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+uint64_t current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+void* SymbolCache::get(const void* symbol) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_status_ptr[dev]) {
+  const uint64_t ctx = current_context_id();
+  std::lock_guard<std::mutex> lock(mu_);
+  Entry& e = entries_[dev];
+  if (e.ptr == nullptr || ctx == 0 || e.ctx != ctx) {
+    // The lookup also creates the device's context if this thread had none yet; its id is read after.
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
-    g_status_ptr[dev] = static_cast<int*>(p);
+    if (cudaGetSymbolAddress(&p, symbol) != cudaSuccess) return nullptr;
+    e.ptr = p;
+    e.ctx = current_context_id();
   }
-  return g_status_ptr[dev];
+  return e.ptr;
 }
+
+static SymbolCache g_status_cache;
+
+int* status_ptr() { return static_cast<int*>(g_status_cache.get(reinterpret_cast<const void*>(&g_device_status))); }
 
 int num_sms() {
   int dev = 0;

@@ -334,22 +334,15 @@ constexpr int kNoAllocMaxParts = kMaxParts;
 
 static __device__ __align__(256) float g_noalloc_dgamma_part[kNoAllocMaxParts * kNoAllocMaxCols];
 
-// Device address of g_noalloc_dgamma_part on each device, looked up once per
-// device (with that device current) by the first call made on it.
-static float* g_noalloc_ptr[64];
-static std::mutex g_noalloc_mu;
+// Device address of g_noalloc_dgamma_part, looked up with the device current by the first call made on
+// that device and cached per device; the cache is keyed on the CUDA context, so a device reset (which
+// reloads the module at a new address) triggers a fresh lookup instead of a stale pointer.
+static SymbolCache g_noalloc_cache;
 
 static int noalloc_scratch(float** out) {
-  int dev = 0;
-  JX_CUDA_TRY(cudaGetDevice(&dev), "jx_rmsnorm_bwd_noalloc: cudaGetDevice");
-  JX_CHECK_ARG(dev >= 0 && dev < 64, "jx_rmsnorm_bwd_noalloc: device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    JX_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_dgamma_part), "jx_rmsnorm_bwd_noalloc: cudaGetSymbolAddress");
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = g_noalloc_cache.get(reinterpret_cast<const void*>(&g_noalloc_dgamma_part));
+  JX_CHECK_ARG(p != nullptr, "jx_rmsnorm_bwd_noalloc: cannot look up the device address of the scratch array");
+  *out = static_cast<float*>(p);
   return JX_OK;
 }
 

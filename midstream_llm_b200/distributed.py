@@ -22,37 +22,45 @@ import torch.distributed as dist
 
 
 class DistributedCapabilityError(RuntimeError):
-    """Raised when a requested topology cannot be supported."""
+    """The requested process topology cannot run here."""
+
+
+# torchrun exports these three together; each maps to one LaunchEnvironment field.
+_TORCHRUN_VARS = {"RANK": "rank", "LOCAL_RANK": "local_rank", "WORLD_SIZE": "world_size"}
 
 
 @dataclass(frozen=True)
 class LaunchEnvironment:
+    """This process's place in the job. A single process (no torchrun variables) is rank 0 of 1."""
     rank: int = 0
     local_rank: int = 0
     world_size: int = 1
 
+    def __post_init__(self) -> None:
+        if self.world_size < 1:
+            raise DistributedCapabilityError(f"WORLD_SIZE must be at least 1 (got {self.world_size})")
+        if self.rank < 0 or self.rank >= self.world_size:
+            raise DistributedCapabilityError(f"RANK {self.rank} is outside [0, {self.world_size})")
+        if self.local_rank < 0:
+            raise DistributedCapabilityError(f"LOCAL_RANK must not be negative (got {self.local_rank})")
+
     @classmethod
     def from_environ(cls, environ: Mapping[str, str] | None = None) -> "LaunchEnvironment":
-        values = os.environ if environ is None else environ
-        keys = ("RANK", "LOCAL_RANK", "WORLD_SIZE")
-        present = [k in values for k in keys]
-        if any(present) and not all(present):
-            missing = ", ".join(k for k, ok in zip(keys, present) if not ok)
-            raise DistributedCapabilityError("incomplete torchrun environment; missing " + missing)
-        if not any(present):
+        """Reads RANK / LOCAL_RANK / WORLD_SIZE: all three or none of them must be set."""
+        source = os.environ if environ is None else environ
+        found = {var: source[var] for var in _TORCHRUN_VARS if var in source}
+        if not found:
             return cls()
-        try:
-            env = cls(rank=int(values["RANK"]), local_rank=int(values["LOCAL_RANK"]),
-                      world_size=int(values["WORLD_SIZE"]))
-        except ValueError as exc:
-            raise DistributedCapabilityError("RANK, LOCAL_RANK, and WORLD_SIZE must be integers") from exc
-        if env.world_size < 1:
-            raise DistributedCapabilityError("WORLD_SIZE must be positive")
-        if not 0 <= env.rank < env.world_size:
-            raise DistributedCapabilityError(f"RANK={env.rank} must be in [0, WORLD_SIZE={env.world_size})")
-        if env.local_rank < 0:
-            raise DistributedCapabilityError("LOCAL_RANK must be non-negative")
-        return env
+        absent = [var for var in _TORCHRUN_VARS if var not in found]
+        if absent:
+            raise DistributedCapabilityError(f"incomplete torchrun environment: {', '.join(absent)} not set")
+        fields = {}
+        for var, text in found.items():
+            try:
+                fields[_TORCHRUN_VARS[var]] = int(text)
+            except ValueError:
+                raise DistributedCapabilityError(f"{var}={text!r} is not an integer") from None
+        return cls(**fields)
 
 
 @dataclass(frozen=True)

@@ -1,9 +1,9 @@
 """Generates the golden fixtures that pin the oracle to the reference.
 
-Run in a checkout where the reference project is available (it is imported
-from MIDSTREAM_REF, default /root/reference/src); the GPU box never runs this.
+Run where the reference project is available; MIDSTREAM_REF must name its
+`src` directory (the one holding the `jishui` package). The GPU box never runs this.
 
-    python tests/golden/make_golden.py
+    MIDSTREAM_REF=<reference checkout>/src python tests/golden/make_golden.py
 
 Writes tests/golden/reference_golden.json with:
   * the tiny debug config's 10-step fp32 AdamW run from the reference package
@@ -26,7 +26,9 @@ import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parents[2]
-REF = os.environ.get("MIDSTREAM_REF", "/root/reference/src")
+REF = os.environ.get("MIDSTREAM_REF")
+if not REF:
+    raise SystemExit("set MIDSTREAM_REF to the reference project's src directory (it holds the jishui package)")
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, REF)
 

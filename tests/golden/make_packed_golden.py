@@ -1,15 +1,22 @@
 """Generates tests/golden/packed_rows.npz: a synthetic multi-shard token index and the rows that the
 reference's own iterators (Midstream-LLM src/jishui/data.py:233-330 PackedBatchIterator,
-:333-379 SequentialBatchIterator) produce from it. Run in a container that has the reference checkout:
+:333-379 SequentialBatchIterator) produce from it. Run where the reference project is available, with
+MIDSTREAM_REF naming its `src` directory (the one holding the `jishui` package):
 
-    PYTHONPATH=/root/reference/src python tests/golden/make_packed_golden.py
+    MIDSTREAM_REF=<reference checkout>/src python tests/golden/make_packed_golden.py
 """
+import os
+import sys
 import tempfile
 from pathlib import Path
 
 import numpy as np
 
-from jishui.data import PackedBatchIterator, PretrainIndex, SequentialBatchIterator
+if not os.environ.get("MIDSTREAM_REF"):
+    raise SystemExit("set MIDSTREAM_REF to the reference project's src directory (it holds the jishui package)")
+sys.path.insert(0, os.environ["MIDSTREAM_REF"])
+
+from jishui.data import PackedBatchIterator, PretrainIndex, SequentialBatchIterator  # noqa: E402
 
 OUT = Path(__file__).resolve().parent / "packed_rows.npz"
 

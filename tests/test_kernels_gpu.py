@@ -291,6 +291,37 @@ def test_cross_entropy(ops):
     assert rel_err(d, lf.grad) < TOL_ATTN
 
 
+@pytest.mark.parametrize("bad", [-5, 32000])
+def test_cross_entropy_rejects_out_of_range_target(ops, bad):
+    """A target outside [0, vocab) that is not ignore_index: torch's cross_entropy refuses it; here the row's
+    loss is NaN (so the mean is NaN and the trainer raises), the device status word reads 202, and the
+    backward gives that row a zero gradient while the other rows keep theirs."""
+    from midstream_llm_b200 import _lib
+    rows, V = 64, 32000
+    _lib.device_status(clear=True)
+    logits = _h(rows, V, scale=3.0, seed=18)
+    t = torch.randint(0, V, (rows,), device="cuda")
+    t[7] = bad
+    lse, row_loss = ops.ce_fwd(logits, t)
+    parts = torch.empty(rows, ops.ce_parts_blocks(V), 2, device="cuda")
+    # The fused path (statistics from the head GEMM's epilogue) follows the same rule.
+    e16 = _h(V, 128, seed=19)
+    h16 = _h(rows, 128, seed=20)
+    lg2, _ = ops.gemm_f16_ce_parts(h16, e16, parts=parts)
+    _, row_loss2 = ops.ce_fwd_parts(parts, lg2, t)
+    lsc = ops.ce_loss(row_loss, t)
+    torch.cuda.synchronize()
+    assert torch.isnan(row_loss[7]) and torch.isnan(row_loss2[7]) and torch.isnan(lsc[2])
+    others = torch.arange(rows, device="cuda") != 7
+    assert torch.isfinite(row_loss[others]).all() and torch.isfinite(row_loss2[others]).all()
+    assert _lib.device_status(clear=True) == 202
+    d = logits.clone()
+    ops.ce_bwd(d, t, lse, torch.tensor([1.0], device="cuda"), torch.tensor([float(rows - 1)], device="cuda"))
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(d[7]) == 0 and torch.count_nonzero(d[8]) > 0
+    assert _lib.device_status(clear=True) == 0
+
+
 def _attn_ref(q, k, v):
     # q,k,v [B,H,T,D] fp32
     T = q.shape[2]
