@@ -1,6 +1,6 @@
 """Training-throughput benchmark of the Jishui decoder step on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload 200m|long]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload 200m|long|base]
 
 One step = one optimizer update. Workloads (token ids Zipf(1.1) from a seed,
 weights N(0, 0.02)):
@@ -10,9 +10,21 @@ weights N(0, 0.02)):
         overlapped with backward; weak scaling).
   long  the same model at seq 4096, micro-batch 4, every layer recomputed in
         backward (gradient checkpointing), grad-accum 1.
-Rank 0 prints one JSON line. `value` times K updates with the batches already
-in HBM; `e2e` times K more through the same public API with each update's
-tokens copied from pinned host memory and the loss read back.
+Rank 0 prints one JSON line:
+  value      K updates with the batches already in HBM (CUDA events, barrier +
+             synchronize around, max over ranks); nothing but the reducer's two
+             overlap events per update is recorded inside that region;
+  e2e        K more through the same public API with each update's tokens copied
+             from pinned host memory and the loss read back;
+  roofline   a third pass of K updates with CUDA events around every GEMM launch
+             (the dominant kernel family), so that instrumentation stays out of
+             `value`;
+  per_gpu_accum1 (1 GPU, workload 200m) K updates of one micro-batch each, the
+             data-parallel runs' per-GPU configuration;
+  exposed_comm_ms_per_step (N > 1) the part of the gradient all-reduce the
+             backward did not hide;
+  gpu_reference (1 GPU) the reference recipe in eager PyTorch on the same GPU;
+  cpu_baseline (1 GPU) the reference update on the host cores.
 `--impl reference` times the reference's update step (the oracle restatement
 of Midstream-LLM's model_torch + pretrain_torch update, fp32, no autocast) on
 the host CPU cores on a bounded sample of the same workload.
@@ -163,6 +175,49 @@ def cpu_reference_rate(steps: int, warmup: int, seq: int, cfg, seed: int = 0) ->
                       f"(oracle restatement of model_torch + pretrain_torch update, no autocast)"}
 
 
+def recompute_flops_per_token(cfg, seq: int) -> float:
+    """Forward FLOPs per token that gradient checkpointing runs a second time (every layer, not the head)."""
+    d, F, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers
+    return 2.0 * L * (4 * d * d + 3 * d * F) + 2.0 * L * seq * d
+
+
+def gpu_reference_rate(cfg, B: int, T: int, accum: int, batches: list, dev) -> dict:
+    """The reference recipe on the same GPU: the oracle's restatement of the reference modules run the way
+    pretrain_torch.py:204-235 runs them (fp16 autocast, torch.amp.GradScaler(65536), torch.optim.AdamW(
+    fused=True), TF32 off, grad clip 1.0), on the workload's micro-batches; tokens/s over 3 timed updates
+    after 2 warm-up updates (CUDA events; the loop's own host reads included, as in the reference)."""
+    from oracle import jishui_ref as oracle
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    ref = oracle.JishuiRef(cfg)
+    oracle.init_weights(ref, 0)
+    ref = ref.to(dev)
+    opt = torch.optim.AdamW(ref.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1, fused=True)
+    scaler = torch.amp.GradScaler("cuda", init_scale=65536.0)
+
+    def upd(b):
+        return oracle.reference_update(ref, opt, scaler, lambda: b, accum, 1.0, 3e-4)
+
+    for b in batches[:2]:
+        upd(b)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for b in batches[2:]:
+        upd(b)
+    e.record()
+    torch.cuda.synchronize()
+    n = len(batches) - 2
+    ms = s.elapsed_time(e) / n
+    rate = B * T * accum / (ms / 1000.0)
+    del ref, opt, scaler
+    torch.cuda.empty_cache()
+    return {"value": rate, "unit": "tokens/s", "ms_per_step": ms, "steps": n,
+            "recipe": "reference modules (oracle restatement) in eager PyTorch: fp16 autocast, cuBLAS GEMMs, "
+                      "F.scaled_dot_product_attention, GradScaler, AdamW(fused=True), TF32 off",
+            "gradient_checkpointing": bool(cfg.gradient_checkpointing)}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -215,6 +270,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=("200m", "long", "base"), default="200m")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-gpu-reference", action="store_true",
+                    help="skip timing the reference recipe (eager torch modules) on the same GPU")
     args = ap.parse_args()
     _keep_stdout_for_result()
     if args.warmup < 3:
@@ -269,7 +326,9 @@ def main() -> None:
         one_update(device_batches(s))
     torch.cuda.synchronize()
 
-    def timed(get_batches, collect_gemm: bool):
+    def timed(get_batches, collect_gemm: bool = False, n_steps: int | None = None, update=None):
+        n_steps = args.steps if n_steps is None else n_steps
+        update = update or one_update
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -279,8 +338,8 @@ def main() -> None:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         results = []
-        for s in range(args.steps):
-            results.append(one_update(get_batches(args.warmup + s)))
+        for s in range(n_steps):
+            results.append(update(get_batches(args.warmup + s)))
         end.record()
         torch.cuda.synchronize()
         ops.set_gemm_profile(None)
@@ -293,20 +352,46 @@ def main() -> None:
             dist.barrier()
         return ms, results, launches, prof
 
+    # 1. The headline value: K updates, batches resident in HBM, no instrumentation inside the timed region
+    #    beyond the communication-overlap events of the data-parallel reducer (two per update).
+    reducer = model.grad_reducer
+    if reducer is not None:
+        reducer.exposed_events = []
     clocks = ClockSampler(dev.index or 0) if rank == 0 else None
     if clocks:
         clocks.start()
-    ms, results, launches, prof = timed(device_batches, collect_gemm=True)
+    ms, results, launches, _ = timed(device_batches)
     clock_info = clocks.stop() if clocks else None
+    exposed_ms = None
+    if reducer is not None:
+        ev = reducer.exposed_events
+        reducer.exposed_events = None
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in ev) / max(args.steps, 1)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        exposed_ms = float(t)
+    # 2. The same updates end to end through the public API: tokens copied from pinned host memory every
+    #    update, the loss read back.
     e2e_ms = None
     if not args.no_e2e:
-        e2e_ms, _, _, _ = timed(host_batches, collect_gemm=False)
+        e2e_ms, _, _, _ = timed(host_batches)
+    # 3. A separate, untimed-for-value pass with every GEMM launch bracketed by CUDA events (the roofline of
+    #    the dominant kernel family).
+    _, _, _, prof = timed(device_batches, collect_gemm=True)
+    # 4. One GPU: the per-GPU rate at grad-accum 1 (the data-parallel runs' per-GPU configuration).
+    accum1_ms = None
+    if world == 1 and accum > 1:
+        def one_micro(batches):
+            return train_update(model, opt, scaler, lambda: batches[:1], 1, 1.0, 3e-4)
+        accum1_ms, _, _, _ = timed(device_batches, update=one_micro)
 
     tokens_per_step = B * T * accum * world
     value = tokens_per_step * args.steps / (ms / 1000.0)
     pk, pk_kind = peaks()
     f_model, f_palm = model_flops_per_token(cfg, T)
     line = None
+    gpu_ref = None
+    if world == 1 and not args.no_gpu_reference:
+        gpu_ref = gpu_reference_rate(cfg, B, T, accum, [device_batches(s) for s in range(2 + 3)], dev)
     if rank == 0:
         gemm_flops = sum(p[0] for p in prof)
         gemm_ms = sum(p[2].elapsed_time(p[3]) for p in prof)
@@ -326,24 +411,37 @@ def main() -> None:
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (Zipf 1.1 tokens, N(0,0.02) weights)",
             "config": {"workload": wl["name"], "model": cfg.name, "global_batch": B * accum * world, "micro_batch": B,
                        "grad_accum": accum, "seq_len": T, "parallelism": f"dp{world}",
+                       "gradient_checkpointing": bool(wl["ckpt"]),
                        "l2": f"working set (activations, {4 * sum(p.numel() for p in model.parameters()) / 1e6:.0f} MB "
                              "fp32 grads) far exceeds the 126 MB L2"},
             "mfu": value * f_model / (world * pk["bf16_tflops"] * 1e12),
             "mfu_palm": value * f_palm / (world * pk["bf16_tflops"] * 1e12),
             "peak_kind": pk_kind,
-            "roofline": {"kernel": "gemm_kernel (tcgen05, all GEMM launches of the timed updates)", "bound": "tensor",
-                         "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
+            "roofline": {"kernel": "gemm_kernel (tcgen05, all GEMM launches of one pass of K updates)",
+                         "bound": "tensor", "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": (gemm_tflops / peak) if gemm_tflops else None, "traffic": traffic,
                          "launches": len(prof), "share_of_step": gemm_ms / ms if ms > 0 else None,
                          "algorithmic_bytes_per_launch": gemm_bytes,
-                         "peak_note": f"bf16_tflops_sustained ({pk_kind})"},
+                         "peak_note": f"bf16_tflops_sustained ({pk_kind}); timed in a separate pass with events "
+                                      "around every GEMM launch"},
             "gpu_launches": launches,
             "clocks": clock_info,
             "loss_last": results[-1]["loss"],
         }
+        if wl["ckpt"]:
+            line["hfu"] = value * (f_model + recompute_flops_per_token(cfg, T)) / (world * pk["bf16_tflops"] * 1e12)
+        if exposed_ms is not None:
+            line["exposed_comm_ms_per_step"] = exposed_ms
+        if accum1_ms is not None:
+            line["per_gpu_accum1"] = {"value": B * T * args.steps / (accum1_ms / 1000.0), "unit": "tokens/s",
+                                      "ms_per_step": accum1_ms / args.steps,
+                                      "note": "the same micro-batch with grad-accum 1 (the data-parallel per-GPU "
+                                              "configuration): optimizer every micro-batch"}
         if e2e_ms is not None:
             line["e2e"] = {"value": tokens_per_step * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
                            "h2d_bytes_per_step": B * (T + 1) * 8 * accum, "d2h_bytes_per_step": 3 * 4}
+        if gpu_ref is not None:
+            line["gpu_reference"] = gpu_ref
         if cpu is not None:
             line["cpu_baseline"] = cpu
         emit(line)

@@ -226,10 +226,14 @@ int jx_ce_bwd(void* logits16, int64_t rows, int vocab, int64_t ld, const int64_t
 /* ---- GradScaler unscale + inf check + global norm, then AdamW ----
  * Stats over a flat gradient buffer (grad_is_f16 selects f16 or f32 input):
  * partial[b] = sum over the block's slice of (g*inv_scale)^2, found_inf set to 1
- * if any element is not finite. nparts = jx_grad_stats_parts(n). */
+ * if any element is not finite. nparts = jx_grad_stats_parts(n).
+ * unscaled_out (f32 [n], may be NULL, may alias an f32 grad) receives
+ * g*inv_scale: GradScaler.unscale_ leaves unscaled gradients in `.grad`, so a
+ * caller's own torch.nn.utils.clip_grad_norm_ sees what it sees in the
+ * reference (pretrain_torch.py:218-219). */
 int jx_grad_stats_parts(int64_t n);
 int jx_grad_stats(const void* grad, int grad_is_f16, int64_t n, const float* inv_scale, float* partial,
-                  float* found_inf, jx_stream_t stream);
+                  float* found_inf, float* unscaled_out, jx_stream_t stream);
 /* total_norm = sqrt(sum partial); clip = min(max_norm/(total_norm+1e-6), 1)
  * (clip_grad_norm_ semantics; max_norm <= 0 disables clipping: clip = 1).
  * out[0] = total_norm, out[1] = clip coefficient. */

@@ -48,7 +48,7 @@ _SIGNATURES: dict[str, tuple] = {
     "jx_ce_loss": (c_int, [_P, _P, c_int64, c_int64, _P, c_int, _P]),
     "jx_ce_bwd": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int64, _P, _P, _P, _P]),
     "jx_grad_stats_parts": (c_int, [c_int64]),
-    "jx_grad_stats": (c_int, [_P, c_int, c_int64, _P, _P, _P, _P]),
+    "jx_grad_stats": (c_int, [_P, c_int, c_int64, _P, _P, _P, _P, _P]),
     "jx_grad_finalize": (c_int, [_P, c_int, c_float, _P, _P]),
     "jx_adamw_step": (c_int, [_P, _P, c_int, _P, _P, _P, c_int64, _P, _P, _P, _P, c_float, c_float, c_float,
                               c_float, c_float, _P]),

@@ -6,9 +6,10 @@
 //   clip_grad_norm_(params, c)   total = ||g||_2, coef = min(c/(total+1e-6), 1), g <- g * coef
 //   scaler.step(opt)             AdamW(fused=True) update unless found_inf
 //   scaler.update()              growth/backoff of the loss scale
-// Here the stats pass reads the raw (scaled) gradients once, the update pass
-// applies (g * inv_scale) * coef on the fly, so unscaled/clipped gradients are
-// never written back to HBM. The AdamW arithmetic follows torch's fused AdamW
+// Here the stats pass reads the raw (scaled) gradients once and, as
+// GradScaler.unscale_ does, writes them back unscaled (so `.grad` holds what
+// torch's own clip_grad_norm_ expects); the clip coefficient is folded into
+// the update pass, so clipped gradients are never written to HBM. The AdamW arithmetic follows torch's fused AdamW
 // (double-precision hyper-parameters, fp32 state): p -= lr*wd*p;
 // m = b1*m + (1-b1)*g; v = b2*v + (1-b2)*g*g;
 // p -= (lr/bc1) * m / (sqrt(v)/sqrt(bc2) + eps).
@@ -52,7 +53,8 @@ template <bool F16>
 __global__ void __launch_bounds__(kThreads) grad_stats_kernel(const void* __restrict__ grad, int64_t n,
                                                               const float* __restrict__ inv_scale,
                                                               float* __restrict__ partial,
-                                                              float* __restrict__ found_inf) {
+                                                              float* __restrict__ found_inf,
+                                                              float* __restrict__ unscaled) {
   const float inv = *inv_scale;
   float ss = 0.f;
   bool bad = false;
@@ -63,15 +65,17 @@ __global__ void __launch_bounds__(kThreads) grad_stats_kernel(const void* __rest
     load_grad4<F16>(grad, i * 4, v);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float u = v[j] * inv;
-      bad |= !isfinite(u);
-      ss += u * u;
+      v[j] *= inv;
+      bad |= !isfinite(v[j]);
+      ss += v[j] * v[j];
     }
+    if (unscaled) reinterpret_cast<float4*>(unscaled)[i] = make_float4(v[0], v[1], v[2], v[3]);
   }
   for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
     const float u = load_grad1<F16>(grad, i) * inv;
     bad |= !isfinite(u);
     ss += u * u;
+    if (unscaled) unscaled[i] = u;
   }
   __shared__ float red[kThreads / 32];
   ss = warp_sum(ss);
@@ -243,15 +247,18 @@ extern "C" int jx_grad_stats_parts(int64_t n) {
 }
 
 extern "C" int jx_grad_stats(const void* grad, int grad_is_f16, int64_t n, const float* inv_scale, float* partial,
-                             float* found_inf, jx_stream_t stream) {
+                             float* found_inf, float* unscaled_out, jx_stream_t stream) {
   JX_CHECK_ARG(grad && inv_scale && partial && found_inf && n > 0, "jx_grad_stats: bad argument");
-  JX_CHECK_ARG(aligned16(grad), "jx_grad_stats: grad must be 16-byte aligned");
+  JX_CHECK_ARG(aligned16(grad) && (!unscaled_out || aligned16(unscaled_out)),
+               "jx_grad_stats: grad and unscaled_out must be 16-byte aligned");
+  JX_CHECK_ARG(!unscaled_out || !grad_is_f16 || (const void*)unscaled_out != grad,
+               "jx_grad_stats: f16 gradients cannot be unscaled in place into f32");
   const int grid = jx_grad_stats_parts(n);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (grad_is_f16)
-    grad_stats_kernel<true><<<grid, kThreads, 0, s>>>(grad, n, inv_scale, partial, found_inf);
+    grad_stats_kernel<true><<<grid, kThreads, 0, s>>>(grad, n, inv_scale, partial, found_inf, unscaled_out);
   else
-    grad_stats_kernel<false><<<grid, kThreads, 0, s>>>(grad, n, inv_scale, partial, found_inf);
+    grad_stats_kernel<false><<<grid, kThreads, 0, s>>>(grad, n, inv_scale, partial, found_inf, unscaled_out);
   JX_CHECK_LAUNCH("jx_grad_stats");
   return JX_OK;
 }

@@ -164,6 +164,10 @@ class GradReducer:
         self._lo = self._hi = None
         self._flat = None
         self.launched: list[tuple[int, int]] = []
+        self.collectives = 0  # all-reduces issued over this reducer's lifetime
+        # When a list, finish() appends (start, end) CUDA events on the compute stream around its wait for
+        # the outstanding buckets: end - start is the communication time the backward did not hide.
+        self.exposed_events: list | None = None
 
     def world_size(self) -> int:
         return dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -180,6 +184,7 @@ class GradReducer:
         work = dist.all_reduce(view, op=op, group=self.group, async_op=True)
         self._works.append((work, view, op))
         self.launched.append((lo, hi))
+        self.collectives += 1
 
     def ready(self, lo: int, hi: int) -> None:
         if not self.enabled or self.world_size() == 1:
@@ -202,8 +207,16 @@ class GradReducer:
             self._launch(self._lo, self._hi)
         self._lo = self._hi = None
         ws = self.world_size()
+        start = end = None
+        if self.exposed_events is not None and self._works and torch.cuda.is_available() and self._flat.g32.is_cuda:
+            start = torch.cuda.Event(enable_timing=True)
+            start.record()
         for work, view, op in self._works:
             work.wait()
             if op == dist.ReduceOp.SUM:
                 view.div_(ws)
+        if start is not None:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            self.exposed_events.append((start, end))
         self._works.clear()

@@ -215,6 +215,30 @@ def bench_attn(iters: int) -> None:
         _emit(f"attn_bwd causal B{B} T{T} H16 D64", _time(lambda: ops.attn_bwd(qkv, o, do, lse, B, T, H, D, out=dqkv,
                                                                               workspace=ws), iters),
               2.5 * fl, "TFLOP/s", pk.get("bf16_tflops", 1590.0))
+        _bench_sdpa(qkv, do, B, T, H, D, fl, iters, pk.get("bf16_tflops", 1590.0))
+
+
+def _bench_sdpa(qkv, do, B, T, H, D, fl, iters, peak) -> None:
+    """torch's F.scaled_dot_product_attention at the same shapes (what the reference calls,
+    model_torch.py:48), with contiguous [B, H, T, D] fp16 operands, for every backend torch offers here."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from torch.nn.functional import scaled_dot_product_attention as sdpa
+    q, k, v = (qkv.view(B, T, 3, H, D)[:, :, i].transpose(1, 2).contiguous().requires_grad_(True) for i in range(3))
+    dout = do.view(B, T, H, D).transpose(1, 2).contiguous()
+    for name, backend in (("default", None), ("flash", SDPBackend.FLASH_ATTENTION),
+                          ("cudnn", SDPBackend.CUDNN_ATTENTION), ("efficient", SDPBackend.EFFICIENT_ATTENTION)):
+        try:
+            ctx = sdpa_kernel(backend) if backend is not None else torch.enable_grad()
+            with ctx:
+                out = sdpa(q, k, v, is_causal=True)
+                tf = _time(lambda: sdpa(q, k, v, is_causal=True), iters)
+                tb = _time(lambda: torch.autograd.grad(out, (q, k, v), dout, retain_graph=True), iters)
+        except Exception as exc:  # a backend that does not support this shape or GPU
+            print(json.dumps({"op": f"torch sdpa[{name}] B{B} T{T}", "unavailable": str(exc).splitlines()[0][:160]}),
+                  flush=True)
+            continue
+        _emit(f"torch sdpa[{name}] fwd causal B{B} T{T} H16 D64", tf, fl, "TFLOP/s", peak)
+        _emit(f"torch sdpa[{name}] bwd causal B{B} T{T} H16 D64", tb, 2.5 * fl, "TFLOP/s", peak)
 
 
 def bench_eval(iters: int) -> None:

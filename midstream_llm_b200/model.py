@@ -72,6 +72,29 @@ def rope_tables(seq_len: int, head_dim: int, theta: float, device) -> tuple[torc
     return angles.cos().contiguous(), angles.sin().contiguous()
 
 
+# Sequence tile of the attention kernels: a batch's rows are padded to a multiple of it. Causal attention
+# never lets a real position see the padding, the padded targets are ignored by the loss, and their
+# logit gradients are zero, so results at the real positions are those of the unpadded sequence.
+_SEQ_TILE = 256
+
+
+def _pad_rows(t: torch.Tensor, fill: int) -> torch.Tensor:
+    """[B, T] integer rows padded on the right to a multiple of the sequence tile with `fill`."""
+    T = t.shape[-1]
+    Tp = -(-T // _SEQ_TILE) * _SEQ_TILE
+    if Tp == T:
+        return t
+    out = torch.full((t.shape[0], Tp), fill, dtype=t.dtype, device=t.device)
+    out[:, :T] = t
+    return out
+
+
+def _unpad_logits(ws: "Workspace", T: int) -> torch.Tensor:
+    """A copy of the workspace logits at the first T positions of each row, [B, T, V]."""
+    full = ws.logits.view(ws.B, ws.T, -1)
+    return full[:, :T].clone() if T != ws.T else full.clone()
+
+
 def check_supported(config: ModelConfig) -> None:
     """Raises for configurations the sm_100a kernels do not implement (no silent fallback)."""
     problems = []
@@ -157,6 +180,7 @@ class FlatParams:
         self.inv_scale: torch.Tensor | None = None
         self.found_inf: torch.Tensor | None = None
         self.clip: torch.Tensor | None = None
+        self.stats_ready = False  # stats_partial holds this update's sums of squares
         self.stats_parts = ops.grad_stats_parts(self.numel)
         self.stats_partial = torch.zeros(self.stats_parts, dtype=torch.float32, device=device)
         self.norm_out = torch.zeros(2, dtype=torch.float32, device=device)
@@ -415,9 +439,9 @@ class JishuiForCausalLM(nn.Module):
 
     def _trunk_fwd(self, ids: torch.Tensor, train: bool, ce: bool = False) -> Workspace:
         c = self.config
-        B, T = ids.shape
-        if T > c.max_position_embeddings:
-            raise ValueError("sequence exceeds configured context length")
+        B, T = ids.shape  # already padded to the sequence tile (callers check the unpadded length)
+        if T % _SEQ_TILE:
+            raise ValueError(f"internal: sequence length {T} is not a multiple of {_SEQ_TILE}")
         fl = self.flat()
         fl.refresh_f16()
         ws = self._workspace(B, T, train)
@@ -444,20 +468,25 @@ class JishuiForCausalLM(nn.Module):
 
     # ---- public forward ------------------------------------------------------
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
-        """logits [B, T, V] in fp16 (model_torch.py:86-98)."""
-        if input_ids.shape[-1] > self.config.max_position_embeddings:
+        """logits [B, T, V] in fp16 (model_torch.py:86-98), for any T up to max_position_embeddings."""
+        T = input_ids.shape[-1]
+        if T > self.config.max_position_embeddings:
             raise ValueError("sequence exceeds configured context length")
-        ids = input_ids.to(torch.int64).contiguous()
+        ids = _pad_rows(input_ids.to(torch.int64).contiguous(), 0)
         if torch.is_grad_enabled() and self.embed_tokens.weight.requires_grad:
-            return _LogitsFn.apply(self, ids, *self.parameters())
+            return _LogitsFn.apply(self, ids, T, *self.parameters())
         ws = self._trunk_fwd(ids, train=False)
-        B, T = ids.shape
-        return ws.logits.clone().view(B, T, -1)
+        return _unpad_logits(ws, T)
 
     def loss(self, inputs: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100) -> torch.Tensor:
-        """Mean cross-entropy of next-token prediction through the fused head."""
-        ids = inputs.to(torch.int64).contiguous()
-        tg = targets.to(torch.int64).contiguous()
+        """Mean cross-entropy of next-token prediction through the fused head (any T up to
+        max_position_embeddings; padded positions are ignored targets)."""
+        if inputs.shape[-1] > self.config.max_position_embeddings:
+            raise ValueError("sequence exceeds configured context length")
+        if targets.shape != inputs.shape:
+            raise ValueError(f"targets {tuple(targets.shape)} and inputs {tuple(inputs.shape)} differ in shape")
+        ids = _pad_rows(inputs.to(torch.int64).contiguous(), 0)
+        tg = _pad_rows(targets.to(torch.int64).contiguous(), ignore_index)
         if torch.is_grad_enabled() and self.embed_tokens.weight.requires_grad:
             return _LossFn.apply(self, ids, tg, ignore_index, *self.parameters())
         ws = self._trunk_fwd(ids, train=False, ce=True)
@@ -476,6 +505,7 @@ class JishuiForCausalLM(nn.Module):
         c = self.config
         fl = self.flat()
         accumulate = fl.prepare_grads()
+        fl.stats_ready, fl.clip = False, None  # the gradients change: earlier norm statistics are stale
         d, V, L = c.hidden_size, c.vocab_size, c.num_hidden_layers
         reducer = self.grad_reducer
         if reducer is not None:
@@ -556,13 +586,12 @@ class _LogitsFn(torch.autograd.Function):
     """forward() under autograd: returns fp16 logits; backward takes dlogits."""
 
     @staticmethod
-    def forward(ctx, model: JishuiForCausalLM, ids, *params):
+    def forward(ctx, model: JishuiForCausalLM, ids, T: int, *params):
         ws = model._trunk_fwd(ids, train=True)
         model._gen += 1
-        ctx.model, ctx.gen, ctx.ws = model, model._gen, ws
+        ctx.model, ctx.gen, ctx.ws, ctx.T = model, model._gen, ws, T
         ctx.save_for_backward(ids)
-        B, T = ids.shape
-        return ws.logits.clone().view(B, T, -1)
+        return _unpad_logits(ws, T)
 
     @staticmethod
     def backward(ctx, dlogits):
@@ -570,9 +599,12 @@ class _LogitsFn(torch.autograd.Function):
         if model._gen != ctx.gen:
             raise RuntimeError("another training forward ran before this backward; activations were overwritten")
         (ids,) = ctx.saved_tensors
-        ws.logits.copy_(dlogits.reshape(ws.logits.shape))
+        B, Tp = ids.shape
+        full = ws.logits.view(B, Tp, -1)
+        full[:, :ctx.T].copy_(dlogits)
+        full[:, ctx.T:].zero_()  # padded positions: no gradient
         model._backward_from_dlogits(ws, ids)
-        return (None, None) + (None,) * (len(ctx.needs_input_grad) - 2)
+        return (None, None, None) + (None,) * (len(ctx.needs_input_grad) - 3)
 
 
 def causal_lm_loss(model: JishuiForCausalLM, inputs: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:

@@ -395,11 +395,18 @@ def ce_bwd(logits16, targets, lse, grad_loss: torch.Tensor, count: torch.Tensor,
 
 
 # ---------------------------------------------------------------- optimizer
-def grad_stats(grad: torch.Tensor, inv_scale: torch.Tensor, partial: torch.Tensor, found_inf: torch.Tensor) -> int:
+def grad_stats(grad: torch.Tensor, inv_scale: torch.Tensor, partial: torch.Tensor, found_inf: torch.Tensor,
+               unscaled_out: torch.Tensor | None = None) -> int:
+    """Per-block sums of (g * inv_scale)^2 into `partial`, found_inf = 1 on a non-finite element; with
+    `unscaled_out` (f32, may be `grad` itself) the unscaled gradients are written there too."""
     n = grad.numel()
     nparts = _lib.query("jx_grad_stats_parts", n)
+    if unscaled_out is not None:
+        _check(unscaled_out, F32, "unscaled_out")
+        if unscaled_out.numel() != n:
+            raise ValueError("unscaled_out must have as many elements as grad")
     _lib.call("jx_grad_stats", grad.data_ptr(), int(grad.dtype == F16), n, inv_scale.data_ptr(), partial.data_ptr(),
-              found_inf.data_ptr(), _stream())
+              found_inf.data_ptr(), _ptr(unscaled_out), _stream())
     return nparts
 
 

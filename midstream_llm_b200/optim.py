@@ -13,11 +13,14 @@ Drop-in for the objects the reference trainer builds
 * `clip_grad_norm_(parameters, max_norm)` — total L2 norm and clip
   coefficient, as torch.nn.utils.clip_grad_norm_ computes them.
 
-Unscaling and clipping are applied inside the fused update: after
-`scaler.unscale_()` / `clip_grad_norm_()` the `.grad` tensors still hold the
-scaled gradients; the factors are held on the device and folded into the
-AdamW pass, so the gradients cross HBM once for the statistics and once for
-the update.
+`scaler.unscale_()` unscales the flat gradient buffer in place in the same
+pass that checks it for non-finite values and sums its squares, so `.grad`
+holds unscaled gradients afterwards, as with torch.amp.GradScaler: the
+reference loop body (pretrain_torch.py:218-219) runs unchanged with
+`torch.nn.utils.clip_grad_norm_`, which rescales `.grad` itself. This
+module's `clip_grad_norm_` instead finishes the norm from the statistics the
+unscale pass already left and folds the clip coefficient into the AdamW pass,
+so the clipped gradients are never written.
 """
 from __future__ import annotations
 
@@ -101,6 +104,7 @@ class AdamW(torch.optim.Optimizer):
                        self._step_state, group["lr"], beta1, beta2, group["eps"], group["weight_decay"])
         flat.mark_f16_current()
         flat.inv_scale = flat.clip = flat.found_inf = None
+        flat.stats_ready = False
         return loss
 
     # -- checkpoint format -------------------------------------------------
@@ -191,8 +195,10 @@ class GradScaler:
         self._lazy(flat.device)
         inv = self._scale.double().reciprocal().float().reshape(1)
         self._found_inf.zero_()
-        ops.grad_stats(flat.g32, inv, flat.stats_partial, self._found_inf)
-        flat.inv_scale, flat.found_inf, flat.clip = inv, self._found_inf, None
+        ops.grad_stats(flat.g32, inv, flat.stats_partial, self._found_inf, unscaled_out=flat.g32)
+        # The buffer now holds unscaled gradients: the update applies no further factor.
+        flat.inv_scale, flat.found_inf, flat.clip = None, self._found_inf, None
+        flat.stats_ready = True
         self._unscaled.add(id(optimizer))
 
     def step(self, optimizer: AdamW, *args, **kwargs):
@@ -247,10 +253,12 @@ def clip_grad_norm_(parameters: Iterable[torch.nn.Parameter], max_norm: float, n
         raise ValueError("only the L2 norm is implemented")
     params = list(parameters)
     flat = _flat_of(params)
-    if flat.inv_scale is None:  # no GradScaler.unscale_ this update: statistics at scale 1
-        flat.inv_scale = torch.ones(1, dtype=torch.float32, device=flat.device)
-        flat.found_inf = torch.zeros(1, dtype=torch.float32, device=flat.device)
-        ops.grad_stats(flat.g32, flat.inv_scale, flat.stats_partial, flat.found_inf)
+    if not flat.stats_ready:  # no GradScaler.unscale_ this update: statistics of the gradients as they are
+        one = torch.ones(1, dtype=torch.float32, device=flat.device)
+        if flat.found_inf is None:
+            flat.found_inf = torch.zeros(1, dtype=torch.float32, device=flat.device)
+        ops.grad_stats(flat.g32, one, flat.stats_partial, flat.found_inf)
+        flat.stats_ready = True
     ops.grad_finalize(flat.stats_partial, flat.stats_parts, float(max_norm), flat.norm_out)
     flat.clip = flat.norm_out[1:2]
     total = flat.norm_out[0].clone()

@@ -39,10 +39,18 @@ def train_update(model: JishuiForCausalLM, optimizer: AdamW, scaler: GradScaler,
         batches = micro_batches()
         if len(batches) != grad_accum_steps:
             raise ValueError(f"expected {grad_accum_steps} micro-batches, got {len(batches)}")
-        for x, y in batches:
+        reducer = model.grad_reducer
+        for i, (x, y) in enumerate(batches):
+            # Data parallel: only the last micro-step's backward all-reduces the accumulated gradients
+            # (the reference's no_sync rule, docs/torch-distributed.md:65); AVG is linear, so the sum of
+            # the micro-steps' gradients is averaged across ranks once.
+            if reducer is not None:
+                reducer.enabled = i == len(batches) - 1
             loss = causal_lm_loss(model, x, y)
             total = loss.detach() if total is None else total + loss.detach()
             scaler.scale(loss / grad_accum_steps).backward()
+        if reducer is not None:
+            reducer.enabled = True
         scaler.unscale_(optimizer)
         grad_norm = clip_grad_norm_(model.parameters(), grad_clip)
         for group in optimizer.param_groups:

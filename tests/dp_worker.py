@@ -56,6 +56,13 @@ def main():
     opt = AdamW(m.parameters(), lr=1e-3, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1)
     scaler = GradScaler("cuda", init_scale=scale)
     r = train_update(m, opt, scaler, lambda: [(x, y)], 1, 1.0, 1e-3)
+    # Gradient accumulation over 2 micro-batches: only the last micro-step's backward all-reduces
+    # (no_sync rule); the update still leaves identical parameters on every rank.
+    per_backward = len(m.grad_reducer.launched)
+    before = m.grad_reducer.collectives
+    x2, y2 = batch(rank + 50, dev)
+    train_update(m, opt, scaler, lambda: [(x, y), (x2, y2)], 2, 1.0, 1e-3)
+    accum_collectives = m.grad_reducer.collectives - before
     flat = torch.cat([p.detach().reshape(-1) for p in m.parameters()])
     gathered = [torch.empty_like(flat) for _ in range(world)]
     dist.all_gather(gathered, flat)
@@ -71,7 +78,7 @@ def main():
             a, b = dp_grads[n].double(), p.grad.double()
             errs[n] = float((a - b).norm() / b.norm().clamp_min(1e-30))
         out = {"world": world, "max_rel_err": max(errs.values()), "errs": errs, "params_agree": params_agree,
-               "attempts": r["attempts"], "buckets": len(m.grad_reducer.launched)}
+               "attempts": r["attempts"], "buckets": per_backward, "accum_collectives": accum_collectives}
         Path(os.environ["DP_TEST_OUT"]).write_text(json.dumps(out))
     dist.barrier()
     ctx.close()

@@ -1,7 +1,8 @@
 """Data-parallel gradients on 2+ GPUs (NCCL, bucketed all-reduce during backward)
 equal one process accumulating every rank's micro-batch with loss / world
-(the DP oracle), within fp16 tolerance; after one update every rank holds
-bit-identical parameters."""
+(the DP oracle), within fp16 tolerance; a grad-accum-2 update all-reduces only
+on its last micro-step; after the updates every rank holds bit-identical
+parameters."""
 import json
 import os
 import socket
@@ -37,3 +38,4 @@ def test_dp_matches_single_process_accumulation(tmp_path):
     assert res["max_rel_err"] < 2e-3, res["errs"]
     assert res["params_agree"]
     assert res["buckets"] > 1
+    assert res["accum_collectives"] == res["buckets"]  # the non-final micro-step issued none

@@ -1,0 +1,280 @@
+"""Whole-model parity at the task's own configurations, on the GPU, against the oracle (the reference
+decoder restated) running the reference's CUDA recipe on identical seeded weights and Zipf(1.1) batches:
+fp16 autocast, torch.amp.GradScaler(65536), torch.optim.AdamW(fused=True), clip 1.0
+(Midstream-LLM src/jishui/pretrain_torch.py:204-235, model_torch.py:76-104).
+
+  * tiny debug config (V 24000, d 256, 4 layers, 4 heads, F 688, seq 256, batch 4, seed 0): every one of
+    10 updates' loss and every parameter's gradient;
+  * the 200M architecture (V 32000, d 1024, 16 layers, F 2816) at micro-batch 16 x 1024: one micro-batch's
+    loss and per-parameter gradients, and the loss after 200 updates (accum 1, cosine warm restarts);
+  * the long-context configuration (seq 4096, micro-batch 4, every layer recomputed): one update;
+  * sequence lengths that are not a multiple of the attention tile (the reference accepts any
+    T <= max_position_embeddings);
+  * the reference loop body itself, unedited (torch.nn.utils.clip_grad_norm_ included), driving the B200
+    model, optimizer and scaler.
+
+Tolerances (the task's): losses rel 2e-3 per update (per-op tolerance), gradients rel 1e-2 norm-wise
+(attention / cross-entropy gradients) -- or, for a parameter whose fp16 rounding noise alone is larger,
+1.5x the reference's own spread between its fp16 recipe and an fp32 run of the same model -- and the loss
+after 200 updates within 0.5 % relative."""
+import copy
+import math
+from dataclasses import replace
+
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle import jishui_ref as oracle
+
+pytestmark = pytest.mark.gpu
+
+LOSS_TOL = 2e-3
+GRAD_TOL = 1e-2
+
+
+def _tiny():
+    from midstream_llm_b200.config import ModelConfig
+    return ModelConfig(name="tiny-debug", vocab_size=24000, hidden_size=256, num_hidden_layers=4,
+                       num_attention_heads=4, num_key_value_heads=4, head_dim=64, intermediate_size=688,
+                       norm_type="rmsnorm", norm_eps=1e-5, norm_bias=False, rope_theta=10000.0,
+                       max_position_embeddings=2048, tie_word_embeddings=True, gradient_checkpointing=False)
+
+
+def _200m(seq=1024, ckpt=False):
+    from midstream_llm_b200.config import jishui_200m
+    return jishui_200m(seq, gradient_checkpointing=ckpt)
+
+
+def _pair(cfg, seed=0):
+    from midstream_llm_b200.model import JishuiForCausalLM
+    torch.manual_seed(seed)
+    ref = oracle.JishuiRef(cfg)
+    oracle.init_weights(ref, seed)
+    mine = JishuiForCausalLM(cfg)
+    mine.load_state_dict(ref.state_dict())
+    return ref.cuda(), mine.cuda()
+
+
+def _batch(cfg, B, T, seed):
+    rows = oracle.zipf_tokens(cfg.vocab_size, B, T, seed).cuda()
+    return rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
+
+
+def _grads(model):
+    return {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+
+
+def _assert_grads(mine_g, ref_g, ref32_g=None, what=""):
+    worst = (None, 0.0)
+    for n, gr in ref_g.items():
+        e = rel_err(mine_g[n], gr)
+        bound = GRAD_TOL if ref32_g is None else max(GRAD_TOL, 1.5 * rel_err(ref32_g[n], gr))
+        assert e < bound, (what, n, e, bound)
+        if e > worst[1]:
+            worst = (n, e)
+    return worst
+
+
+def _update_with_grads(model, opt, scaler, x, y, loss_fn, lr, autocast):
+    """One update as pretrain_torch.py:204-235 runs it at grad-accum 1, returning (loss, unscaled grads)."""
+    opt.zero_grad(set_to_none=True)
+    if autocast:
+        with torch.autocast("cuda", dtype=torch.float16):
+            loss = loss_fn(model, x, y)
+    else:
+        loss = loss_fn(model, x, y)
+    scaler.scale(loss).backward()
+    scaler.unscale_(opt)
+    grads = _grads(model)
+    grad_norm = torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+    for group in opt.param_groups:
+        group["lr"] = lr
+    assert torch.isfinite(grad_norm)
+    scaler.step(opt)
+    scaler.update()
+    return float(loss), grads
+
+
+def _optimizers(ref, mine):
+    from midstream_llm_b200 import AdamW, GradScaler
+    r_opt = torch.optim.AdamW(ref.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1, fused=True)
+    r_sc = torch.amp.GradScaler("cuda", init_scale=65536.0)
+    m_opt = AdamW(mine.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1, fused=True)
+    m_sc = GradScaler("cuda", init_scale=65536.0)
+    return r_opt, r_sc, m_opt, m_sc
+
+
+def test_tiny_config_ten_updates_losses_and_gradients():
+    """BASELINE's tiny debug config: 10 updates, each update's loss and every parameter's gradient."""
+    from midstream_llm_b200.model import causal_lm_loss
+    cfg = _tiny()
+    ref, mine = _pair(cfg, 0)
+    r_opt, r_sc, m_opt, m_sc = _optimizers(ref, mine)
+    for step in range(10):
+        x, y = _batch(cfg, 4, 256, step)
+        rl, rg = _update_with_grads(ref, r_opt, r_sc, x, y, oracle.causal_lm_loss, 3e-4, True)
+        ml, mg = _update_with_grads(mine, m_opt, m_sc, x, y, causal_lm_loss, 3e-4, False)
+        assert abs(ml - rl) / rl < LOSS_TOL, (step, ml, rl)
+        _assert_grads(mg, rg, what=f"update {step}")
+    for (n, a), (_, b) in zip(mine.named_parameters(), ref.named_parameters()):
+        assert rel_err(a, b) < 1e-3, n
+
+
+@pytest.mark.slow
+def test_200m_micro_batch_loss_and_gradients():
+    """The 200M architecture at micro-batch 16 x 1024 (BASELINE's step): loss and every parameter gradient."""
+    from midstream_llm_b200.model import causal_lm_loss
+    cfg = _200m()
+    ref, mine = _pair(cfg, 0)
+    x, y = _batch(cfg, 16, 1024, 1)
+    scale = 65536.0
+    with torch.autocast("cuda", dtype=torch.float16):
+        rl = oracle.causal_lm_loss(ref, x, y)
+    (rl * scale).backward()
+    rg = _grads(ref)
+    ref.zero_grad(set_to_none=True)
+    ref32 = ref.float()
+    (oracle.causal_lm_loss(ref32, x, y) * scale).backward()
+    r32 = _grads(ref32)
+    del ref, ref32
+    torch.cuda.empty_cache()
+    ml = causal_lm_loss(mine, x, y)
+    (ml * scale).backward()
+    mg = _grads(mine)
+    assert abs(float(ml) - float(rl)) / float(rl) < LOSS_TOL
+    _assert_grads(mg, rg, r32, what="200M")
+
+
+@pytest.mark.slow
+def test_200m_loss_after_200_updates():
+    """200 updates of the 200M model at micro-batch 16 x 1024, accum 1, cosine warm restarts (warmup 20,
+    2 cycles): the mean loss of the last 10 updates within 0.5 % of the reference recipe's."""
+    from midstream_llm_b200 import train_update
+    from midstream_llm_b200.config import TrainConfig
+    from midstream_llm_b200.schedules import continuation_lr, make_continuation_schedule
+    cfg = _200m()
+    sched = make_continuation_schedule({"schedule": "cosine_warm_restarts", "cycles": 2},
+                                       TrainConfig(learning_rate=3e-4, min_learning_rate=3e-5, warmup_steps=20),
+                                       0, 200, 3e-5)
+    batches = [_batch(cfg, 16, 1024, 1000 + s) for s in range(200)]
+    ref, mine = _pair(cfg, 0)
+    r_opt, r_sc, m_opt, m_sc = _optimizers(ref, mine)
+    ref_losses = [oracle.reference_update(ref, r_opt, r_sc, lambda: [batches[s]], 1, 1.0,
+                                          continuation_lr(sched, s))["loss"] for s in range(200)]
+    del ref, r_opt, r_sc
+    torch.cuda.empty_cache()
+    my_losses = [train_update(mine, m_opt, m_sc, lambda: [batches[s]], 1, 1.0, continuation_lr(sched, s))["loss"]
+                 for s in range(200)]
+    assert abs(my_losses[0] - ref_losses[0]) / ref_losses[0] < LOSS_TOL
+    tail_ref, tail_me = sum(ref_losses[-10:]) / 10, sum(my_losses[-10:]) / 10
+    assert abs(tail_me - tail_ref) / tail_ref < 5e-3, (tail_me, tail_ref)
+    assert my_losses[-1] < my_losses[0] - 2.0  # it learns
+
+
+@pytest.mark.slow
+def test_long_context_recompute_update():
+    """Seq 4096, micro-batch 4, every layer recomputed in backward: one update's loss and gradients, then
+    the parameters after the update."""
+    from midstream_llm_b200.model import causal_lm_loss
+    cfg = _200m(4096, ckpt=True)
+    ref, mine = _pair(cfg, 0)
+    ref.train()
+    ref32 = copy.deepcopy(ref).float()
+    x, y = _batch(cfg, 4, 4096, 2)
+    (oracle.causal_lm_loss(ref32, x, y) * 65536.0).backward()
+    r32 = _grads(ref32)
+    del ref32
+    torch.cuda.empty_cache()
+    r_opt, r_sc, m_opt, m_sc = _optimizers(ref, mine)
+    rl, rg = _update_with_grads(ref, r_opt, r_sc, x, y, oracle.causal_lm_loss, 3e-4, True)
+    ml, mg = _update_with_grads(mine, m_opt, m_sc, x, y, causal_lm_loss, 3e-4, False)
+    assert abs(ml - rl) / rl < LOSS_TOL
+    _assert_grads(mg, rg, {n: g / 65536.0 for n, g in r32.items()}, what="seq 4096")
+    for (n, a), (_, b) in zip(mine.named_parameters(), ref.named_parameters()):
+        assert rel_err(a, b) < 1e-4, n
+
+
+@pytest.mark.parametrize("B,T", [(2, 300), (3, 7), (1, 1000)])
+def test_sequence_lengths_off_the_tile(B, T):
+    """forward() logits, the loss and every gradient at T not a multiple of the attention tile."""
+    from midstream_llm_b200.model import causal_lm_loss
+    cfg = replace(_tiny(), vocab_size=4096, num_hidden_layers=2)
+    ref, mine = _pair(cfg, 3)
+    x, y = _batch(cfg, B, T, 5)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.float16):
+        ref_logits = ref(x)
+    with torch.no_grad():
+        logits = mine(x)
+    assert logits.shape == ref_logits.shape == (B, T, cfg.vocab_size)
+    assert rel_err(logits, ref_logits) < 2e-3
+    with torch.autocast("cuda", dtype=torch.float16):
+        rl = oracle.causal_lm_loss(ref, x, y)
+    (rl * 1024.0).backward()
+    ml = causal_lm_loss(mine, x, y)
+    (ml * 1024.0).backward()
+    assert abs(float(ml) - float(rl)) / float(rl) < 1e-3
+    _assert_grads(_grads(mine), _grads(ref), what=f"T={T}")
+    # forward() under autograd: gradients through the returned logits (padded positions get none)
+    mine.zero_grad(set_to_none=True)
+    ref.zero_grad(set_to_none=True)
+    w = torch.randn(B, T, cfg.vocab_size, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    with torch.autocast("cuda", dtype=torch.float16):
+        (ref(x).float() * w).sum().backward()
+    (mine(x).float() * w).sum().backward()
+    _assert_grads(_grads(mine), _grads(ref), what=f"forward() T={T}")
+
+
+def _reference_loop_body(model, optimizer, scaler, micro, accum, grad_clip, lr, loss_fn):
+    """pretrain_torch.py:205-235 as written there (sampler replay aside): the loop a caller of the reference
+    runs, here handed the B200 model, AdamW and GradScaler."""
+    for attempt in range(8):
+        optimizer.zero_grad(set_to_none=True)
+        total_loss = 0.0
+        for x, y in micro:
+            with torch.autocast("cuda", dtype=torch.float16):
+                loss = loss_fn(model, x, y)
+            if not torch.isfinite(loss):
+                raise FloatingPointError("non-finite loss")
+            total_loss += float(loss.detach())
+            scaler.scale(loss / accum).backward()
+        scaler.unscale_(optimizer)
+        grad_norm = torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip)
+        for group in optimizer.param_groups:
+            group["lr"] = lr
+        if not torch.isfinite(grad_norm):
+            scaler.update(new_scale=scaler.get_scale() / 2)
+            continue
+        scaler.step(optimizer)
+        scaler.update()
+        return {"loss": total_loss / accum, "grad_norm": float(grad_norm), "attempts": attempt + 1}
+    raise FloatingPointError("gradient overflow persisted after 8 retries")
+
+
+@pytest.mark.parametrize("init_scale", [65536.0, 2.0 ** 24])
+def test_reference_loop_body_runs_unchanged(init_scale):
+    """The reference's own loop body (with torch.nn.utils.clip_grad_norm_, not this library's) on the B200
+    objects gives what train_update gives: after unscale_ the .grad tensors hold unscaled gradients, so
+    torch's clip sees the true norm. The large initial scale forces overflow retries on both."""
+    from midstream_llm_b200 import AdamW, GradScaler, JishuiForCausalLM, causal_lm_loss, train_update
+    cfg = replace(_tiny(), vocab_size=4096, num_hidden_layers=2)
+    ref, a = _pair(cfg, 4)
+    b = JishuiForCausalLM(cfg).cuda()
+    b.load_state_dict(a.state_dict())
+    opts = [AdamW(m.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1, fused=True) for m in (a, b)]
+    scalers = [GradScaler("cuda", init_scale=init_scale) for _ in range(2)]
+    for step in range(3):
+        micro = [_batch(cfg, 2, 256, 40 + 2 * step + i) for i in range(2)]
+        ra = train_update(a, opts[0], scalers[0], lambda: micro, 2, 1.0, 3e-4)
+        rb = _reference_loop_body(b, opts[1], scalers[1], micro, 2, 1.0, 3e-4, causal_lm_loss)
+        assert ra["attempts"] == rb["attempts"]
+        assert ra["loss"] == pytest.approx(rb["loss"], rel=1e-6)
+        assert ra["grad_norm"] == pytest.approx(rb["grad_norm"], rel=1e-4)
+        assert scalers[0].get_scale() == scalers[1].get_scale()
+    if init_scale > 65536.0:
+        assert scalers[0].get_scale() < init_scale  # the retries really happened
+    for (n, pa), (_, pb) in zip(a.named_parameters(), b.named_parameters()):
+        assert rel_err(pb, pa) < 1e-5, n
+    for p in a.parameters():  # .grad is unscaled after unscale_: its norm is the reported grad norm's scale
+        assert torch.isfinite(p.grad).all()
+    assert math.isfinite(ra["grad_norm"])
