@@ -153,6 +153,15 @@ int64_t jx_gemm_wgrad_workspace_bytes(int N, int K, int splits);
  * per host thread (it affects only calls made from the thread that set it),
  * and both kernels give identical results. */
 int jx_gemm_set_mode(int mode);
+/* Failure-detection test hook (no counterpart in the reference: it exercises this
+ * library's bounded waits). Runs the 1-SM GEMM kernel on one 128 x 256 x 64 tile
+ * (A [128][64], B [256][64], C [128][256] f16) with its TMA loads withheld, so the
+ * MMA thread's wait for the first operand stage expires after wait_budget_cycles
+ * (clock64 cycles, at most 2^32; the production kernels allow 2^32, about 2 s).
+ * The kernel then records 102 in the device status word (jx_device_status), every
+ * warp leaves through the normal teardown and C is left unwritten; the context
+ * stays usable. */
+int jx_gemm_wait_test(const void* A, const void* B, void* C, int64_t wait_budget_cycles, jx_stream_t stream);
 int jx_gemm_wgrad(const void* dY, int64_t lddy, const void* X, int64_t ldx, int T, int N, int K, float* G,
                   int64_t ldg, int accumulate, int splits, void* workspace, jx_stream_t stream);
 

@@ -37,6 +37,7 @@ _SIGNATURES: dict[str, tuple] = {
     "jx_gemm_swiglu_bwd": (c_int, [_P, c_int64, _P, c_int, c_int, c_int, _P, _P, c_int64, _P, c_int64, _P]),
     "jx_gemm_wgrad_workspace_bytes": (c_int64, [c_int, c_int, c_int]),
     "jx_gemm_set_mode": (c_int, [c_int]),
+    "jx_gemm_wait_test": (c_int, [_P, _P, _P, c_int64, _P]),
     "jx_gemm_wgrad": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, c_int, _P, c_int64, c_int, c_int, _P, _P]),
     "jx_attn_fwd_workspace_bytes": (c_int64, [c_int, c_int, c_int, c_int]),
     "jx_attn_fwd": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_float, _P]),

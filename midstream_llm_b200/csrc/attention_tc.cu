@@ -98,6 +98,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // Work distribution of the persistent forward. Work items are numbered in
 // chunks of whole (head, batch) pairs; inside a chunk the heaviest items of all
@@ -337,7 +344,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
         if (!diag) {
 #pragma unroll
-          for (int i = 0; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[i]));
+          for (int i = 0; i < BKV; i += 2)
+            mp[(i >> 1) & 7] = max3(mp[(i >> 1) & 7], __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
         } else {
 #pragma unroll
           for (int i = 0; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], i <= lim ? __uint_as_float(sr[i]) : -INFINITY);
@@ -353,33 +361,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           m = m_cand;
           rescale = true;
         }
-        // P = exp2(s*scale - m) as fp16 pairs (64 registers) and 8 partial row sums, computed before waiting
-        // for the previous tile's P V: the exponentials overlap that product instead of following it.
-        float sp[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) sp[u] = 0.f;
-        const float neg_m = -m;
-        uint32_t pw[64];
-#pragma unroll
-        for (int e = 0; e < 64; ++e) {
-          const int i0 = 2 * e;
-          float p0 = ex2(fmaf(__uint_as_float(sr[i0]), scale_log2, neg_m));
-          float p1 = ex2(fmaf(__uint_as_float(sr[i0 + 1]), scale_log2, neg_m));
-          if (diag) {
-            if (i0 > lim) p0 = 0.f;
-            if (i0 + 1 > lim) p1 = 0.f;
-          }
-          sp[(2 * e) & 7] += p0;
-          sp[(2 * e + 1) & 7] += p1;
-          __half2 hp = __floats2half2_rn(p0, p1);
-          pw[e] = *reinterpret_cast<uint32_t*>(&hp);
-        }
         // P V of the previous tile must be done before P is overwritten or O is rescaled
         // (for j = 0 the previous item's epilogue waited for it).
         if (j > 0 && !warp_wait(&bars->p_empty[w], (g - 1) & 1, abort_flag, status, kFaSoftmax)) { ok = false; break; }
         tc_fence_after();
-        tmem_st32(lane_base + 128, *reinterpret_cast<uint32_t(*)[32]>(&pw[0]));
-        tmem_st32(lane_base + 160, *reinterpret_cast<uint32_t(*)[32]>(&pw[32]));
+        // P = exp2(s*scale - m) as fp16 pairs into TMEM (64 columns, two stores of 32); 8 partial row sums.
+        // (Computing all exponentials before this wait needs 64 more live registers and spills; measured slower.)
+        float sp[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sp[u] = 0.f;
+        const float neg_m = -m;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t pw[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int i0 = hf * 64 + 2 * e;
+            float p0 = ex2(fmaf(__uint_as_float(sr[i0]), scale_log2, neg_m));
+            float p1 = ex2(fmaf(__uint_as_float(sr[i0 + 1]), scale_log2, neg_m));
+            if (diag) {
+              if (i0 > lim) p0 = 0.f;
+              if (i0 + 1 > lim) p1 = 0.f;
+            }
+            sp[(2 * e) & 7] += p0;
+            sp[(2 * e + 1) & 7] += p1;
+            __half2 hp = __floats2half2_rn(p0, p1);
+            pw[e] = *reinterpret_cast<uint32_t*>(&hp);
+          }
+          tmem_st32(lane_base + 128 + hf * 32, pw);
+        }
         const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
         // Rare: bring the TMEM output to the new max.
         if (__any_sync(0xffffffffu, rescale)) {

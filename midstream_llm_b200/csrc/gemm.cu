@@ -76,18 +76,20 @@ struct Params {
   int accumulate;
   float* ws;
   int* status;
+  long long wait_budget;  // clock64 cycles a barrier wait may take before the kernel gives up (~2 s)
+  int skip_loads;         // test hook (jx_gemm_wait_test): the producer issues no loads
 };
 
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, const Params& p,
                                          int code) {
-  long long start = clock64();
+  const long long start = clock64();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 255u) {
       if (*abort_flag) return false;
-      if (clock64() - start > (1ll << 32)) {
+      if (clock64() - start > p.wait_budget) {
         *abort_flag = 1;
-        if (status) atomicExch(status, code);
+        if (p.status) atomicExch(p.status, code);
         return false;
       }
     }
@@ -96,10 +98,10 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 
 // Warp-wide wait where only lane 0 polls (all 32 lanes active); the accumulator
 // it guards lives in TMEM, read after tcgen05.fence::after_thread_sync.
-__device__ __forceinline__ bool warp_wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                              int code) {
+__device__ __forceinline__ bool warp_wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              const Params& p, int code) {
   int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = wait_bar(bar, parity, abort_flag, status, code) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = wait_bar(bar, parity, abort_flag, p, code) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   __syncwarp();
   return ok != 0;
@@ -415,7 +417,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
     const int pos = p.rope_seq > 0 ? row % p.rope_seq : 0;
     // Staged: the caller requested this warp's cos / sin box (rows yrow % rope_seq .. +31, 128B-swizzled).
     if (aux && nb * BN + half * 128 < p.rope_cols) {
-      if (!warp_wait_bar(aux->bar, aux->phase, aux->abort_flag, p.status, kStatusGemmEpilogueWait)) return;
+      if (!warp_wait_bar(aux->bar, aux->phase, aux->abort_flag, p, kStatusGemmEpilogueWait)) return;
       aux->phase ^= 1u;
     }
 #pragma unroll 1
@@ -521,7 +523,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
       if (aux) {
         // The caller requested this tile's first box; this warp requests the second as soon as
         // the first is in registers, so its load overlaps the arithmetic below.
-        if (!warp_wait_bar(aux->bar, aux->phase, aux->abort_flag, p.status, kStatusGemmEpilogueWait)) return;
+        if (!warp_wait_bar(aux->bar, aux->phase, aux->abort_flag, p, kStatusGemmEpilogueWait)) return;
         aux->phase ^= 1u;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -635,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = p.tiles_m * p.tiles_n * p.splits;
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane == 0 && !p.skip_loads) {
       uint32_t it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -646,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const uint32_t stage = it % STAGES;
           const uint32_t parity = ((it / STAGES) & 1u) ^ 1u;
-          if (!wait_bar(&empty[stage], parity, abort_flag, p.status, kStatusGemmProducerWait)) {
+          if (!wait_bar(&empty[stage], parity, abort_flag, p, kStatusGemmProducerWait)) {
             ok = false;
             break;
           }
@@ -685,12 +687,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb0 = s * p.kb_per_split;
         const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         const int acc = local & 1;
-        if (!wait_bar(&acc_empty[acc], ((local >> 1) & 1) ^ 1, abort_flag, p.status, kStatusGemmMmaWait)) break;
+        if (!wait_bar(&acc_empty[acc], ((local >> 1) & 1) ^ 1, abort_flag, p, kStatusGemmMmaWait)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const uint32_t stage = it % STAGES;
-          if (!wait_bar(&full[stage], (it / STAGES) & 1u, abort_flag, p.status, kStatusGemmMmaWait)) {
+          if (!wait_bar(&full[stage], (it / STAGES) & 1u, abort_flag, p, kStatusGemmMmaWait)) {
             ok = false;
             break;
           }
@@ -720,7 +722,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int mb, nb, s;
       tile_coords(p, t, mb, nb, s);
       const int acc = local & 1;
-      if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
+      if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
       epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb, nb, s);
       tc_fence_before();
@@ -900,7 +902,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const uint32_t stage = it % S2;
-          if (!wait_bar(&empty[stage], ((it / S2) & 1u) ^ 1u, abort_flag, p.status, kStatusGemmProducerWait)) {
+          if (!wait_bar(&empty[stage], ((it / S2) & 1u) ^ 1u, abort_flag, p, kStatusGemmProducerWait)) {
             ok = false;
             break;
           }
@@ -941,12 +943,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb0 = s * p.kb_per_split;
         const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         const int acc = local & 1;
-        if (!wait_bar(&acc_empty[acc], ((local >> 1) & 1) ^ 1, abort_flag, p.status, kStatusGemmMmaWait)) break;
+        if (!wait_bar(&acc_empty[acc], ((local >> 1) & 1) ^ 1, abort_flag, p, kStatusGemmMmaWait)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const uint32_t stage = it % S2;
-          if (!wait_bar(&full[stage], (it / S2) & 1u, abort_flag, p.status, kStatusGemmMmaWait)) {
+          if (!wait_bar(&full[stage], (it / S2) & 1u, abort_flag, p, kStatusGemmMmaWait)) {
             ok = false;
             break;
           }
@@ -988,7 +990,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int y = (mb2 * 2 + (int)rank) * BM + quarter * 32;
         if (p.rope_tma && nb * BN + half * 128 < p.rope_cols && lane == 0) aux.issue(0, y % p.rope_seq);
       }
-      if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p.status, kStatusGemmEpilogueWait)) break;
+      if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
       epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb2 * 2 + (int)rank, nb, s,
                          (EPI == kSwigluB || (EPI == kRope && p.rope_tma)) ? &aux : nullptr);
@@ -1219,7 +1221,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
     ok = make_tmap_f16(&ta, A, p.M, p.K, lda, 64, BK);
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for A", name);
   const int b_rows = (EPI == kSwigluF) ? 2 * p.swiglu_F : p.N;
-  const bool two_sm = (g_gemm_mode == 2) || (g_gemm_mode == 0 && p.M > BM);
+  const bool two_sm = !p.skip_loads && ((g_gemm_mode == 2) || (g_gemm_mode == 0 && p.M > BM));
   if (!B_MN)
     ok = make_tmap_f16(&tb, B, p.K, b_rows, ldb, BK, (EPI == kSwigluF || two_sm) ? 128 : BN);
   else
@@ -1319,6 +1321,7 @@ static Params base_params(int M, int N, int K) {
   p.N = N;
   p.K = K;
   p.splits = 1;
+  p.wait_budget = 1ll << 32;
   return p;
 }
 
@@ -1456,4 +1459,20 @@ extern "C" int jx_gemm_set_mode(int mode) {
   JX_CHECK_ARG(mode >= 0 && mode <= 2, "jx_gemm_set_mode: mode must be 0 (auto), 1 (1-SM) or 2 (2-SM)");
   jx::gemm::g_gemm_mode = mode;
   return JX_OK;
+}
+
+extern "C" int jx_gemm_wait_test(const void* A, const void* B, void* C, int64_t wait_budget_cycles,
+                                 jx_stream_t stream) {
+  JX_CHECK_ARG(C && aligned16(C), "jx_gemm_wait_test: C must be 16-byte aligned");
+  JX_CHECK_ARG(wait_budget_cycles > 0 && wait_budget_cycles <= (1ll << 32),
+               "jx_gemm_wait_test: wait budget must be in (0, 2^32] cycles");
+  // One 128 x 256 x 64 tile on the 1-SM kernel with its TMA loads withheld: the MMA thread's wait for the
+  // first stage runs out, sets the abort flag and the status word, and every warp leaves through the
+  // normal teardown (no copy is in flight, the TMEM is released).
+  Params p = base_params(128, 256, 64);
+  p.C = static_cast<__half*>(C);
+  p.ldc = 256;
+  p.wait_budget = wait_budget_cycles;
+  p.skip_loads = 1;
+  return launch<kF16, false, false>(A, 64, B, 64, p, reinterpret_cast<cudaStream_t>(stream), "jx_gemm_wait_test");
 }
