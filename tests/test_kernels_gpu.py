@@ -20,9 +20,10 @@ def ops():
     return _ops
 
 
-@pytest.fixture(params=[1, 2], ids=["1sm", "2sm"])
+@pytest.fixture(params=[0, 1, 2], ids=["auto", "1sm", "2sm"])
 def gemm_mode(request, ops):
-    """Runs a GEMM test once with the 1-SM kernel and once with the 2-SM (CTA pair) kernel."""
+    """Runs a GEMM test with the library's own kernel choice (the default path), the 1-SM kernel and the
+    2-SM (CTA pair) kernel."""
     from midstream_llm_b200 import _lib
     _lib.call("jx_gemm_set_mode", request.param)
     yield request.param
