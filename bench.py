@@ -270,6 +270,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=("200m", "long", "base"), default="200m")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sm-reserve", type=int, default=int(os.environ.get("JX_SM_RESERVE", "0")),
+                    help="SMs the persistent kernels leave to NCCL while gradient buckets are in flight (N > 1)")
     ap.add_argument("--no-gpu-reference", action="store_true",
                     help="skip timing the reference recipe (eager torch modules) on the same GPU")
     args = ap.parse_args()
@@ -301,7 +303,7 @@ def main() -> None:
     opt = AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1, fused=True)
     scaler = GradScaler("cuda", init_scale=65536.0)
     if world > 1:
-        model.grad_reducer = GradReducer(bucket_bytes=25 * 1024 * 1024)
+        model.grad_reducer = GradReducer(bucket_bytes=25 * 1024 * 1024, sm_reserve=args.sm_reserve)
 
     stream = ZipfBatches(cfg.vocab_size, B, T, seed=1000 + rank)
     n_host = (args.warmup + args.steps) * accum
@@ -425,6 +427,7 @@ def main() -> None:
                          "peak_note": f"bf16_tflops_sustained ({pk_kind}); timed in a separate pass with events "
                                       "around every GEMM launch"},
             "gpu_launches": launches,
+            "sm_reserve": args.sm_reserve if world > 1 else 0,
             "clocks": clock_info,
             "loss_last": results[-1]["loss"],
         }

@@ -56,6 +56,11 @@ int64_t jx_launch_count(void);
  * bounded wait expired (code identifies the wait). Reads and optionally clears
  * it; synchronises the current device. */
 int jx_device_status(int* status_out, int clear);
+/* Number of SMs that the persistent kernels (GEMM, attention) launched from the
+ * calling host thread leave free, e.g. for NCCL's collective kernels while
+ * gradient buckets are in flight during a data-parallel backward (0 by default,
+ * at most 64; results do not depend on it). No counterpart in the reference. */
+int jx_set_sm_reserve(int sms);
 
 /* ---- RMSNorm (model_torch.py:12-15, nn.RMSNorm, eps from ModelConfig.norm_eps) ----
  * Forward: s = x (+ resid if resid != NULL, stored to sum_out as f16);

@@ -18,6 +18,7 @@ _SIGNATURES: dict[str, tuple] = {
     "jx_last_error": (ctypes.c_char_p, []),
     "jx_launch_count": (c_int64, []),
     "jx_device_status": (c_int, [ctypes.POINTER(c_int), c_int]),
+    "jx_set_sm_reserve": (c_int, [c_int]),
     "jx_rmsnorm_fwd": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, c_int, c_float, _P]),
     "jx_rmsnorm_bwd_parts": (c_int, [c_int64]),
     "jx_rmsnorm_bwd": (c_int, [_P, _P, _P, _P, _P, _P, _P, c_int64, c_int, _P]),

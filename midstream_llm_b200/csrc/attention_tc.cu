@@ -970,7 +970,7 @@ extern "C" int jx_attn_fwd(const void* qkv, void* out, float* lse, void* workspa
   JX_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int), s), "jx_attn_fwd: clear work counter");
   const float scale_log2 = scale * 1.4426950408889634f;
   const int64_t items = (int64_t)(T / (2 * BQ)) * H * B;
-  const int grid = (int)std::min<int64_t>(items, num_sms());
+  const int grid = (int)std::min<int64_t>(items, persistent_sms());
   attn_fwd_tc_kernel<<<grid, kFwdThreads, kSmemBytes, s>>>(tm, static_cast<__half*>(out), lse, counter, B, T, H,
                                                            scale_log2, status_ptr());
   JX_CHECK_LAUNCH("jx_attn_fwd");
@@ -1026,7 +1026,7 @@ extern "C" int jx_attn_bwd(const void* qkv, const void* out, const void* dout, c
               }),
               "jx_attn_bwd: smem attribute");
   const int64_t items = (int64_t)(T / BQ) * H * B;
-  const int grid = (int)std::min<int64_t>(items, num_sms());
+  const int grid = (int)std::min<int64_t>(items, persistent_sms());
   attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(tq, tdo, tdq, nl2, delta, dq_acc, static_cast<__half*>(dqkv),
                                                         counter, B, T, H, scale, scale * 1.4426950408889634f,
                                                         rope_cos, rope_sin, status_ptr());

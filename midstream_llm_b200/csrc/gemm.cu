@@ -1293,7 +1293,8 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
       JX_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, gemm2_kernel<EPI, A_MN, B_MN>, &cfg), name);
       slot.store(n > 0 ? n : 1, std::memory_order_release);
     }
-    const int max_cl = slot.load(std::memory_order_acquire);
+    int max_cl = slot.load(std::memory_order_acquire);
+    if (max_cl > persistent_sms() / 2) max_cl = persistent_sms() / 2;
     const int tiles2 = ((p.tiles_m + 1) / 2) * p.tiles_n * p.splits;
     const int clusters = tiles2 < max_cl ? tiles2 : max_cl;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
@@ -1308,7 +1309,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
               }),
               name);
   const int tiles = p.tiles_m * p.tiles_n * p.splits;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int grid = tiles < persistent_sms() ? tiles : persistent_sms();
   gemm_kernel<EPI, A_MN, B_MN><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tc0, tc1, tc2, p);
   JX_CHECK_LAUNCH(name);
   return JX_OK;

@@ -89,7 +89,21 @@ int num_sms() {
   return g_sms[dev];
 }
 
+// SMs a host thread leaves free for other work while its persistent kernels run (jx_set_sm_reserve).
+static thread_local int g_sm_reserve = 0;
+
+int persistent_sms() {
+  const int n = num_sms() - g_sm_reserve;
+  return n < 8 ? 8 : n;
+}
+
 }  // namespace jx
+
+extern "C" int jx_set_sm_reserve(int sms) {
+  JX_CHECK_ARG(sms >= 0 && sms <= 64, "jx_set_sm_reserve: reserve must be in [0, 64] (got %d)", sms);
+  jx::g_sm_reserve = sms;
+  return JX_OK;
+}
 
 extern "C" int jx_version(void) { return 100; }
 

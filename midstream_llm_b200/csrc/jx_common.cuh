@@ -50,6 +50,8 @@ void count_launch();
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int num_sms();
+// SMs the persistent kernels of the calling host thread may occupy: num_sms() minus its reserve.
+int persistent_sms();
 
 // ---------------------------------------------------------------------------
 // Small device utilities.

@@ -156,8 +156,11 @@ class GradReducer:
     for non-final gradient-accumulation micro-steps.
     """
 
-    def __init__(self, group=None, bucket_bytes: int = 25 * 1024 * 1024):
+    def __init__(self, group=None, bucket_bytes: int = 25 * 1024 * 1024, sm_reserve: int = 0):
         self.group = group
+        # SMs the persistent GEMM / attention kernels leave to NCCL while buckets are in flight.
+        self.sm_reserve = int(sm_reserve)
+        self._reserving = False
         self.bucket_elems = max(1, bucket_bytes // 4)
         self.enabled = True
         self._works: list = []
@@ -178,7 +181,14 @@ class GradReducer:
         self._lo = self._hi = None
         self.launched = []
 
+    def _set_reserve(self, on: bool) -> None:
+        if self.sm_reserve and on != self._reserving and self._flat is not None and self._flat.g32.is_cuda:
+            from . import _lib
+            _lib.call("jx_set_sm_reserve", self.sm_reserve if on else 0)
+            self._reserving = on
+
     def _launch(self, lo: int, hi: int) -> None:
+        self._set_reserve(True)
         view = self._flat.g32[lo:hi]
         op = dist.ReduceOp.AVG if dist.get_backend(self.group) == "nccl" else dist.ReduceOp.SUM
         work = dist.all_reduce(view, op=op, group=self.group, async_op=True)
@@ -220,3 +230,4 @@ class GradReducer:
             end.record()
             self.exposed_events.append((start, end))
         self._works.clear()
+        self._set_reserve(False)
