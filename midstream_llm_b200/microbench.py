@@ -166,9 +166,12 @@ def bench_adamw(iters: int) -> None:
           pk["hbm_gbs"], bytes_per_param=2, update_skipped=skipped)
 
 
-def bench_gemm(iters: int) -> None:
-    pk = _peaks()
-    from .model import rope_tables
+def gemm_cases():
+    """Every GEMM call of one micro-batch of the 200M step (16 x 1024 tokens), issued as the model issues it
+    (same entry points, operand majors, epilogues and split-K counts). Each case: (name, launches per
+    micro-batch, FLOPs, algorithmic bytes -- operands read once, outputs written once, an accumulated fp32
+    gradient read and written --, the call)."""
+    from .model import _wgrad_splits, rope_tables
     M, d, F, V = 16384, 1024, 2816, 32000
     hh = lambda *s: (torch.randn(*s, device="cuda") * 0.5).half()  # noqa: E731
     x, wqkv, wo, wgu, wd, E = hh(M, d), hh(3 * d, d), hh(d, d), hh(2 * F, d), hh(d, F), hh(V, d)
@@ -176,26 +179,58 @@ def bench_gemm(iters: int) -> None:
     qkv = torch.empty(M, 3 * d, device="cuda", dtype=torch.half)
     gt, up, act = (torch.empty(M, F, device="cuda", dtype=torch.half) for _ in range(3))
     out = torch.empty(M, d, device="cuda", dtype=torch.half)
+    out2 = torch.empty(M, d, device="cuda", dtype=torch.half)
     dgu = torch.empty(M, 2 * F, device="cuda", dtype=torch.half)
+    dq = hh(M, 3 * d)
     logits = torch.empty(M, V, device="cuda", dtype=torch.half)
-    G = torch.zeros(2 * F, d, device="cuda")
+    parts = torch.empty(M, ops.ce_parts_blocks(V), 2, device="cuda")
+    gqkv, go, ggu, gd = (torch.zeros(n, k, device="cuda") for n, k in ((3 * d, d), (d, d), (2 * F, d), (d, F)))
     GV = torch.zeros(V, d, device="cuda")
     ws = torch.empty(64 << 20, device="cuda")
-    peak = pk.get("bf16_tflops", 1590.0)
-    cases = [
-        ("qkv+rope [16384x3072x1024]", 2 * M * 3 * d * d, lambda: ops.gemm_qkv_rope(x, wqkv, d, cos, sin, 1024, 64, out=qkv)),
-        ("o_proj+residual [16384x1024x1024]", 2 * M * d * d, lambda: ops.gemm_f16(x, wo, resid=x, out=out)),
-        ("gate|up+swiglu [16384x5632x1024]", 2 * M * 2 * F * d, lambda: ops.gemm_swiglu_fwd(x, wgu, F, gate=gt, up=up, act=act)),
-        ("down+residual [16384x1024x2816]", 2 * M * d * F, lambda: ops.gemm_f16(act, wd, resid=x, out=out)),
-        ("lm_head [16384x32000x1024]", 2 * M * V * d, lambda: ops.gemm_f16(x, E, out=logits)),
-        ("down dgrad+swiglu bwd [16384x2816x1024]", 2 * M * F * d, lambda: ops.gemm_swiglu_bwd(x, wd, gt, up, out=dgu)),
-        ("gate|up dgrad [16384x1024x5632]", 2 * M * 2 * F * d, lambda: ops.gemm_f16(dgu, wgu, b_mn_major=True, out=out)),
-        ("head dgrad [16384x1024x32000]", 2 * M * V * d, lambda: ops.gemm_f16(logits, E, b_mn_major=True, out=out)),
-        ("gate|up wgrad [5632x1024, 16384 tokens]", 2 * M * 2 * F * d, lambda: ops.gemm_wgrad(dgu, x, G, True, 3, ws)),
-        ("head wgrad [32000x1024, 16384 tokens]", 2 * M * V * d, lambda: ops.gemm_wgrad(logits, x, GV, True, 1, ws)),
+    sp = lambda n, k: _wgrad_splits(n, k, M)  # noqa: E731
+    b16 = lambda *n: 2.0 * sum(n)  # noqa: E731
+    wg = lambda n, k: 2.0 * M * (n + k) + 8.0 * n * k  # noqa: E731  (accumulated fp32 gradient: read + write)
+    return [
+        ("qkv+rope [16384x3072x1024]", 16, 2 * M * 3 * d * d, b16(M * d, 3 * d * d, M * 3 * d),
+         lambda: ops.gemm_qkv_rope(x, wqkv, d, cos, sin, 1024, 64, out=qkv)),
+        ("o_proj+residual [16384x1024x1024]", 16, 2 * M * d * d, b16(M * d, d * d, 2 * M * d),
+         lambda: ops.gemm_f16(x, wo, resid=x, out=out)),
+        ("gate|up+swiglu [16384x5632x1024]", 16, 2 * M * 2 * F * d, b16(M * d, 2 * F * d, 3 * M * F),
+         lambda: ops.gemm_swiglu_fwd(x, wgu, F, gate=gt, up=up, act=act)),
+        ("down+residual [16384x1024x2816]", 16, 2 * M * d * F, b16(M * F, d * F, 2 * M * d),
+         lambda: ops.gemm_f16(act, wd, resid=x, out=out)),
+        ("tied head + CE statistics [16384x32000x1024]", 1, 2 * M * V * d, b16(M * d, V * d, M * V),
+         lambda: ops.gemm_f16_ce_parts(x, E, out=logits, parts=parts)),
+        ("down dgrad+swiglu bwd [16384x2816x1024]", 16, 2 * M * F * d, b16(M * d, F * d, 4 * M * F),
+         lambda: ops.gemm_swiglu_bwd(x, wd, gt, up, out=dgu)),
+        (f"down wgrad [1024x2816, 16384 tokens, {sp(d, F)} splits]", 16, 2 * M * d * F, wg(d, F),
+         lambda: ops.gemm_wgrad(out, act, gd, True, sp(d, F), ws)),
+        ("gate|up dgrad [16384x1024x5632]", 16, 2 * M * 2 * F * d, b16(M * 2 * F, 2 * F * d, M * d),
+         lambda: ops.gemm_f16(dgu, wgu, b_mn_major=True, out=out)),
+        (f"gate|up wgrad [5632x1024, 16384 tokens, {sp(2 * F, d)} splits]", 16, 2 * M * 2 * F * d, wg(2 * F, d),
+         lambda: ops.gemm_wgrad(dgu, x, ggu, True, sp(2 * F, d), ws)),
+        ("o dgrad [16384x1024x1024]", 16, 2 * M * d * d, b16(M * d, d * d, M * d),
+         lambda: ops.gemm_f16(out, wo, b_mn_major=True, out=out2)),
+        (f"o wgrad [1024x1024, 16384 tokens, {sp(d, d)} splits]", 16, 2 * M * d * d, wg(d, d),
+         lambda: ops.gemm_wgrad(out, x, go, True, sp(d, d), ws)),
+        ("qkv dgrad [16384x1024x3072]", 16, 2 * M * 3 * d * d, b16(M * 3 * d, 3 * d * d, M * d),
+         lambda: ops.gemm_f16(dq, wqkv, b_mn_major=True, out=out)),
+        (f"qkv wgrad [3072x1024, 16384 tokens, {sp(3 * d, d)} splits]", 16, 2 * M * 3 * d * d, wg(3 * d, d),
+         lambda: ops.gemm_wgrad(dq, x, gqkv, True, sp(3 * d, d), ws)),
+        ("head dgrad [16384x1024x32000]", 1, 2 * M * V * d, b16(M * V, V * d, M * d),
+         lambda: ops.gemm_f16(logits, E, b_mn_major=True, out=out)),
+        ("head wgrad [32000x1024, 16384 tokens]", 1, 2 * M * V * d, wg(V, d),
+         lambda: ops.gemm_wgrad(logits, x, GV, True, 1, ws)),
     ]
-    for name, fl, fn in cases:
-        _emit("gemm " + name, _time(fn, iters), fl, "TFLOP/s", peak, peak_kind="bf16_tflops (burst)")
+
+
+def bench_gemm(iters: int) -> None:
+    """The step's GEMM calls one after another (3 warm-up + `iters` timed launches each)."""
+    pk = _peaks()
+    peak = pk.get("bf16_tflops", 1590.0)
+    for name, per_mb, fl, nbytes, fn in gemm_cases():
+        _emit("gemm " + name, _time(fn, iters), fl, "TFLOP/s", peak, peak_kind="bf16_tflops (burst)",
+              launches_per_microbatch=per_mb, algorithmic_bytes=nbytes)
 
 
 def bench_attn(iters: int) -> None:
