@@ -272,6 +272,9 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--sm-reserve", type=int, default=int(os.environ.get("JX_SM_RESERVE", "0")),
                     help="SMs the persistent kernels leave to NCCL while gradient buckets are in flight (N > 1)")
+    ap.add_argument("--shard-optimizer", type=int, default=int(os.environ.get("JX_SHARD_OPTIMIZER", "1")),
+                    help="N > 1: reduce each gradient bucket to its owning rank, update 1/N of the parameters "
+                         "per rank and all-gather the fp16 weights (1) instead of all-reducing (0)")
     ap.add_argument("--no-gpu-reference", action="store_true",
                     help="skip timing the reference recipe (eager torch modules) on the same GPU")
     args = ap.parse_args()
@@ -303,7 +306,8 @@ def main() -> None:
     opt = AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1, fused=True)
     scaler = GradScaler("cuda", init_scale=65536.0)
     if world > 1:
-        model.grad_reducer = GradReducer(bucket_bytes=25 * 1024 * 1024, sm_reserve=args.sm_reserve)
+        model.grad_reducer = GradReducer(bucket_bytes=25 * 1024 * 1024, sm_reserve=args.sm_reserve,
+                                         shard_optimizer=bool(args.shard_optimizer))
 
     stream = ZipfBatches(cfg.vocab_size, B, T, seed=1000 + rank)
     n_host = (args.warmup + args.steps) * accum
@@ -412,7 +416,10 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (Zipf 1.1 tokens, N(0,0.02) weights)",
             "config": {"workload": wl["name"], "model": cfg.name, "global_batch": B * accum * world, "micro_batch": B,
-                       "grad_accum": accum, "seq_len": T, "parallelism": f"dp{world}",
+                       "grad_accum": accum, "seq_len": T,
+                       "parallelism": f"dp{world}" + (" (25 MB buckets reduced to their owning rank, sharded AdamW, "
+                                                      "fp16 weights all-gathered)" if world > 1 and args.shard_optimizer
+                                                      else ""),
                        "gradient_checkpointing": bool(wl["ckpt"]),
                        "l2": f"working set (activations, {4 * sum(p.numel() for p in model.parameters()) / 1e6:.0f} MB "
                              "fp32 grads) far exceeds the 126 MB L2"},
@@ -428,6 +435,7 @@ def main() -> None:
                                       "around every GEMM launch"},
             "gpu_launches": launches,
             "sm_reserve": args.sm_reserve if world > 1 else 0,
+            "sharded_update": bool(args.shard_optimizer) and world > 1,
             "clocks": clock_info,
             "loss_last": results[-1]["loss"],
         }

@@ -144,33 +144,100 @@ def initialize_runtime(plan: RuntimePlan, timeout_s: float | None = None) -> Run
 
 
 class GradReducer:
-    """Averages the flat fp32 gradient buffer across ranks while backward runs.
+    """Reduces the flat fp32 gradient buffer across ranks while backward runs.
 
     The decoder's backward calls `ready(lo, hi)` each time a contiguous range
     of the flat gradient buffer is final (the final norm, then each layer from
     the last to the first, then the tied embedding). Ranges are merged into
-    buckets of about `bucket_bytes` and each bucket is all-reduced (AVG)
-    asynchronously on NCCL's stream as soon as it fills, so communication of
-    layer l overlaps the backward of layers l-1..0. `finish()` makes the
-    compute stream wait for every outstanding bucket. Set `enabled = False`
-    for non-final gradient-accumulation micro-steps.
+    buckets of about `bucket_bytes`, each launched asynchronously on NCCL's
+    stream as soon as it fills, so communication of layer l overlaps the
+    backward of layers l-1..0. `finish()` makes the compute stream wait for
+    every outstanding bucket. Set `enabled = False` for non-final
+    gradient-accumulation micro-steps.
+
+    Two modes:
+      * replicated (default): every bucket is all-reduced (AVG); every rank then
+        holds the mean gradient and runs the whole optimizer update;
+      * sharded (`shard_optimizer=True`, a ZeRO-1-style update): the flat buffer
+        is split into `world_size` equal contiguous shards; each bucket piece is
+        reduced (SUM) to the rank that owns it, which is about half an
+        all-reduce's traffic. GradScaler.unscale_ folds the 1/world_size of the
+        mean into its unscale pass over the local shard and all-reduces only
+        its partial sums of squares and the inf flag; AdamW updates the local
+        shard and all-gathers the fp16 weights in place. Each rank's fp32 master
+        weights and moments are current on its own shard only:
+        `gather_full_state(optimizer)` (a collective: every rank calls it)
+        makes them whole again, e.g. before rank 0 writes a checkpoint.
     """
 
-    def __init__(self, group=None, bucket_bytes: int = 25 * 1024 * 1024, sm_reserve: int = 0):
+    def __init__(self, group=None, bucket_bytes: int = 25 * 1024 * 1024, sm_reserve: int = 0,
+                 shard_optimizer: bool = False):
         self.group = group
         # SMs the persistent GEMM / attention kernels leave to NCCL while buckets are in flight.
         self.sm_reserve = int(sm_reserve)
         self._reserving = False
+        self.shard_optimizer = bool(shard_optimizer)
         self.bucket_elems = max(1, bucket_bytes // 4)
         self.enabled = True
         self._works: list = []
         self._lo = self._hi = None
         self._flat = None
         self.launched: list[tuple[int, int]] = []
-        self.collectives = 0  # all-reduces issued over this reducer's lifetime
+        self.collectives = 0  # gradient collectives issued over this reducer's lifetime
         # When a list, finish() appends (start, end) CUDA events on the compute stream around its wait for
         # the outstanding buckets: end - start is the communication time the backward did not hide.
         self.exposed_events: list | None = None
+
+    # ---- sharding ---------------------------------------------------------
+    def sharded(self) -> bool:
+        return self.shard_optimizer and self.world_size() > 1
+
+    def shard_size(self, numel: int) -> int:
+        n = self.world_size()
+        if numel % n:
+            raise ValueError(f"flat buffer of {numel} elements does not split into {n} equal shards")
+        return numel // n
+
+    def shard_range(self, flat) -> tuple[int, int]:
+        """[lo, hi) of the flat buffers that this rank updates."""
+        size = self.shard_size(flat.numel)
+        r = dist.get_rank(self.group)
+        return r * size, (r + 1) * size
+
+    def pieces(self, lo: int, hi: int, numel: int) -> list[tuple[int, int, int]]:
+        """[lo, hi) cut at shard boundaries: (owner rank in the group, start, end) per piece."""
+        size = self.shard_size(numel)
+        out = []
+        a = lo
+        while a < hi:
+            owner = a // size
+            b = min(hi, (owner + 1) * size)
+            out.append((owner, a, b))
+            a = b
+        return out
+
+    def reduce_stats(self, partial: torch.Tensor, found_inf: torch.Tensor) -> None:
+        """Sums the shards' partial sums of squares and inf flags across ranks (stream-ordered)."""
+        dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
+        dist.all_reduce(found_inf, op=dist.ReduceOp.SUM, group=self.group)
+
+    def gather_f16(self, flat) -> None:
+        """All ranks' updated fp16 shards into every rank's fp16 weight copy (in place)."""
+        lo, hi = self.shard_range(flat)
+        dist.all_gather_into_tensor(flat.p16, flat.p16[lo:hi], group=self.group)
+
+    def gather_full_state(self, optimizer=None) -> None:
+        """Makes the fp32 master weights (and the optimizer's moments) whole on every rank. A collective."""
+        flat = self._flat if optimizer is None else optimizer._ensure_state()
+        if not self.sharded() or flat is None:
+            return
+        lo, hi = self.shard_range(flat)
+        bufs = [flat.p32]
+        if optimizer is not None and optimizer._m is not None:
+            bufs += [optimizer._m, optimizer._v]
+        for b in bufs:
+            dist.all_gather_into_tensor(b, b[lo:hi].clone(), group=self.group)
+        flat.mark_f16_current()
 
     def world_size(self) -> int:
         return dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -189,6 +256,15 @@ class GradReducer:
 
     def _launch(self, lo: int, hi: int) -> None:
         self._set_reserve(True)
+        if self.sharded():
+            for owner, a, b in self.pieces(lo, hi, self._flat.numel):
+                dst = owner if self.group is None else dist.get_global_rank(self.group, owner)
+                work = dist.reduce(self._flat.g32[a:b], dst=dst, op=dist.ReduceOp.SUM, group=self.group,
+                                   async_op=True)
+                self._works.append((work, None, None))
+                self.collectives += 1
+            self.launched.append((lo, hi))
+            return
         view = self._flat.g32[lo:hi]
         op = dist.ReduceOp.AVG if dist.get_backend(self.group) == "nccl" else dist.ReduceOp.SUM
         work = dist.all_reduce(view, op=op, group=self.group, async_op=True)

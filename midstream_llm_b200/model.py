@@ -37,6 +37,9 @@ from . import _lib, ops
 from .config import ModelConfig
 
 _ALIGN = 64
+# The flat buffers are padded to a multiple of this many elements, so that 1, 2, 4 or 8 data-parallel ranks
+# get equal contiguous shards that start on 64-element (256-byte) boundaries.
+_SHARD_ALIGN = 512
 
 # Parameter -> weak reference to the JishuiForCausalLM that owns it; lets the
 # optimizer, GradScaler and clip_grad_norm_ find the model's flat buffers from
@@ -163,11 +166,11 @@ class FlatParams:
         for n, p in named:
             self.offsets[n] = off
             off += _round_up(p.numel())
-        self.numel = off
+        self.numel = _round_up(off, _SHARD_ALIGN)
         self.device = device
-        self.p32 = torch.zeros(off, dtype=torch.float32, device=device)
-        self.g32 = torch.zeros(off, dtype=torch.float32, device=device)
-        self.p16 = torch.zeros(off, dtype=torch.float16, device=device)
+        self.p32 = torch.zeros(self.numel, dtype=torch.float32, device=device)
+        self.g32 = torch.zeros(self.numel, dtype=torch.float32, device=device)
+        self.p16 = torch.zeros(self.numel, dtype=torch.float16, device=device)
         with torch.no_grad():
             for n, p in named:
                 view = self.p32_view(n, p.shape)
@@ -183,6 +186,7 @@ class FlatParams:
         self.stats_ready = False  # stats_partial holds this update's sums of squares
         self.stats_parts = ops.grad_stats_parts(self.numel)
         self.stats_partial = torch.zeros(self.stats_parts, dtype=torch.float32, device=device)
+        self.stats_count = self.stats_parts  # partial sums written by the last statistics pass
         self.norm_out = torch.zeros(2, dtype=torch.float32, device=device)
         self.refresh_f16(force=True)
 

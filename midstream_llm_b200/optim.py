@@ -38,6 +38,27 @@ def _flat_of(params):
     return owner_of(params).flat()
 
 
+def _shard_reducer(flat):
+    """The model's GradReducer when it runs the sharded (ZeRO-1-style) update, else None."""
+    from .model import owner_of
+    red = owner_of(flat.params[:1]).grad_reducer
+    return red if red is not None and red.sharded() else None
+
+
+def _stats_pass(flat, inv: torch.Tensor, found_inf: torch.Tensor, write_back: bool) -> None:
+    """Sum of squares of g * inv (per-block partials in flat.stats_partial) and the inf flag, optionally
+    writing g * inv back. Sharded: over this rank's shard, with the 1/world_size of the mean folded into
+    inv, then the partials and the flag are summed across ranks."""
+    red = _shard_reducer(flat)
+    lo, hi = (0, flat.numel) if red is None else red.shard_range(flat)
+    if red is not None:
+        inv = inv / red.world_size()
+    g = flat.g32[lo:hi]
+    flat.stats_count = ops.grad_stats(g, inv, flat.stats_partial, found_inf, unscaled_out=g if write_back else None)
+    if red is not None:
+        red.reduce_stats(flat.stats_partial[:flat.stats_count], found_inf)
+
+
 class AdamW(torch.optim.Optimizer):
     """torch.optim.AdamW(fused=True) semantics over the flat parameter buffer."""
 
@@ -100,8 +121,13 @@ class AdamW(torch.optim.Optimizer):
                 return loss
             flat.prepare_grads()  # zero-fill parameters that received no gradient
         beta1, beta2 = group["betas"]
-        ops.adamw_step(flat.p32, flat.g32, self._m, self._v, flat.p16, flat.inv_scale, flat.clip, flat.found_inf,
-                       self._step_state, group["lr"], beta1, beta2, group["eps"], group["weight_decay"])
+        red = _shard_reducer(flat)
+        lo, hi = (0, flat.numel) if red is None else red.shard_range(flat)
+        ops.adamw_step(flat.p32[lo:hi], flat.g32[lo:hi], self._m[lo:hi], self._v[lo:hi], flat.p16[lo:hi],
+                       flat.inv_scale, flat.clip, flat.found_inf, self._step_state, group["lr"], beta1, beta2,
+                       group["eps"], group["weight_decay"])
+        if red is not None:  # every rank's updated fp16 shard to every rank
+            red.gather_f16(flat)
         flat.mark_f16_current()
         flat.inv_scale = flat.clip = flat.found_inf = None
         flat.stats_ready = False
@@ -195,7 +221,7 @@ class GradScaler:
         self._lazy(flat.device)
         inv = self._scale.double().reciprocal().float().reshape(1)
         self._found_inf.zero_()
-        ops.grad_stats(flat.g32, inv, flat.stats_partial, self._found_inf, unscaled_out=flat.g32)
+        _stats_pass(flat, inv, self._found_inf, write_back=True)
         # The buffer now holds unscaled gradients: the update applies no further factor.
         flat.inv_scale, flat.found_inf, flat.clip = None, self._found_inf, None
         flat.stats_ready = True
@@ -257,9 +283,10 @@ def clip_grad_norm_(parameters: Iterable[torch.nn.Parameter], max_norm: float, n
         one = torch.ones(1, dtype=torch.float32, device=flat.device)
         if flat.found_inf is None:
             flat.found_inf = torch.zeros(1, dtype=torch.float32, device=flat.device)
-        ops.grad_stats(flat.g32, one, flat.stats_partial, flat.found_inf)
+        # Sharded updates reduce gradient sums: the mean's 1/world_size is written into the shard here.
+        _stats_pass(flat, one, flat.found_inf, write_back=_shard_reducer(flat) is not None)
         flat.stats_ready = True
-    ops.grad_finalize(flat.stats_partial, flat.stats_parts, float(max_norm), flat.norm_out)
+    ops.grad_finalize(flat.stats_partial, flat.stats_count, float(max_norm), flat.norm_out)
     flat.clip = flat.norm_out[1:2]
     total = flat.norm_out[0].clone()
     if error_if_nonfinite and not bool(torch.isfinite(total)):

@@ -67,6 +67,32 @@ def main():
     gathered = [torch.empty_like(flat) for _ in range(world)]
     dist.all_gather(gathered, flat)
     params_agree = all(torch.equal(g, gathered[0]) for g in gathered)
+    # The sharded (ZeRO-1-style) update: this rank's shard of the gradients is reduced to it, AdamW runs on
+    # the shard, the fp16 weights are all-gathered. Compared against the replicated update from the same
+    # start: gradients on the own shard, fp16 weights everywhere, master weights after gather_full_state.
+    ms = model_on(dev)
+    ms.grad_reducer = GradReducer(bucket_bytes=1 << 20, shard_optimizer=True)
+    mr = model_on(dev)
+    mr.grad_reducer = GradReducer(bucket_bytes=1 << 20)
+    opt_s = AdamW(ms.parameters(), lr=1e-3, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1)
+    opt_r = AdamW(mr.parameters(), lr=1e-3, betas=(0.9, 0.95), eps=1e-5, weight_decay=0.1)
+    sc_s, sc_r = GradScaler("cuda", init_scale=scale), GradScaler("cuda", init_scale=scale)
+    x3, y3 = batch(rank + 70, dev)
+    rs = train_update(ms, opt_s, sc_s, lambda: [(x3, y3)], 1, 1.0, 1e-3)
+    rr = train_update(mr, opt_r, sc_r, lambda: [(x3, y3)], 1, 1.0, 1e-3)
+    fs, fr = ms.flat(), mr.flat()
+    lo, hi = ms.grad_reducer.shard_range(fs)
+    shard_grad_err = float((fs.g32[lo:hi] - fr.g32[lo:hi]).norm() / fr.g32[lo:hi].norm())
+    g16 = [torch.empty_like(fs.p16) for _ in range(world)]
+    dist.all_gather(g16, fs.p16)
+    f16_equal_ranks = all(torch.equal(g, g16[0]) for g in g16)
+    f16_err = float((fs.p16.float() - fr.p16.float()).norm() / fr.p16.float().norm())
+    ms.grad_reducer.gather_full_state(opt_s)
+    p32_err = float((fs.p32 - fr.p32).norm() / fr.p32.norm())
+    m_err = float((opt_s._m - opt_r._m).norm() / opt_r._m.norm())
+    sharded = {"shard_grad_err": shard_grad_err, "f16_equal_ranks": f16_equal_ranks, "f16_err": f16_err,
+               "p32_err": p32_err, "m_err": m_err, "grad_norm": [rs["grad_norm"], rr["grad_norm"]],
+               "loss": [rs["loss"], rr["loss"]]}
     if rank == 0:
         ref = model_on(dev)
         for rr in range(world):
@@ -78,7 +104,8 @@ def main():
             a, b = dp_grads[n].double(), p.grad.double()
             errs[n] = float((a - b).norm() / b.norm().clamp_min(1e-30))
         out = {"world": world, "max_rel_err": max(errs.values()), "errs": errs, "params_agree": params_agree,
-               "attempts": r["attempts"], "buckets": per_backward, "accum_collectives": accum_collectives}
+               "attempts": r["attempts"], "buckets": per_backward, "accum_collectives": accum_collectives,
+               "sharded": sharded}
         Path(os.environ["DP_TEST_OUT"]).write_text(json.dumps(out))
     dist.barrier()
     ctx.close()

@@ -84,6 +84,61 @@ def test_grad_reducer_gloo_two_ranks():
         assert n >= 6  # 16448 elements in buckets of <= 3000
 
 
+class _FakeFlatN:
+    def __init__(self, n, rank):
+        g = torch.Generator().manual_seed(100 + rank)
+        self.g32 = torch.randn(n, generator=g)
+        self.numel = n
+
+
+def _sharded_worker(rank, world, port, out_q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from midstream_llm_b200.distributed import GradReducer
+        n = 16448  # a bucket (3000 elements) straddles the shard boundary at 8224
+        flat = _FakeFlatN(n, rank)
+        total = sum(_FakeFlatN(n, r).g32 for r in range(world))
+        red = GradReducer(bucket_bytes=3000 * 4, shard_optimizer=True)
+        red.begin(flat)
+        for lo, hi in _RANGES:
+            red.ready(lo, hi)
+        red.finish()
+        lo, hi = red.shard_range(flat)
+        ok = torch.allclose(flat.g32[lo:hi], total[lo:hi], rtol=1e-6, atol=1e-6)
+        pieces = red.pieces(7000, 10000, n)
+        split_ok = pieces == [(0, 7000, 8224), (1, 8224, 10000)]
+        covered = sorted(red.launched)
+        full = covered[0][0] == 0 and covered[-1][1] == n
+        dist.barrier()
+        dist.destroy_process_group()
+        out_q.put((rank, ok, split_ok, full, (lo, hi), red.collectives))
+    except Exception:
+        out_q.put((rank, "error", traceback.format_exc()))
+
+
+def test_sharded_reducer_gloo_two_ranks():
+    """The sharded update's gradient exchange: every bucket is cut at the shard boundary and each piece is
+    reduced (summed) to the rank that owns it; each rank then holds the exact sum on its own shard."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    shards = set()
+    for r in results:
+        assert r[1] != "error", r[2]
+        rank, ok, split_ok, full, rng, collectives = r
+        assert ok and split_ok and full, r
+        assert collectives > len(_RANGES)  # straddling buckets became two reductions
+        shards.add(rng)
+    assert shards == {(0, 8224), (8224, 16448)}
+
+
 def _dead_rank_worker(rank, world, port, out_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime

@@ -2,7 +2,9 @@
 equal one process accumulating every rank's micro-batch with loss / world
 (the DP oracle), within fp16 tolerance; a grad-accum-2 update all-reduces only
 on its last micro-step; after the updates every rank holds bit-identical
-parameters."""
+parameters. The sharded (ZeRO-1-style) update matches the replicated one: the
+gradients of each rank's own shard, the fp16 weights on every rank, and the
+master weights and moments once gathered."""
 import json
 import os
 import socket
@@ -39,3 +41,8 @@ def test_dp_matches_single_process_accumulation(tmp_path):
     assert res["params_agree"]
     assert res["buckets"] > 1
     assert res["accum_collectives"] == res["buckets"]  # the non-final micro-step issued none
+    sh = res["sharded"]
+    assert sh["shard_grad_err"] < 1e-6, sh  # reduce-to-owner sums equal the all-reduce on the own shard
+    assert sh["f16_equal_ranks"], sh
+    assert sh["f16_err"] < 1e-3 and sh["p32_err"] < 1e-6 and sh["m_err"] < 1e-5, sh
+    assert abs(sh["grad_norm"][0] - sh["grad_norm"][1]) <= 1e-5 * sh["grad_norm"][1], sh
