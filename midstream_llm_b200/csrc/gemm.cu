@@ -196,7 +196,42 @@ __device__ __forceinline__ void to_f32(const uint32_t (&r)[32], float (&v)[32]) 
 // division; the results are rounded to fp16, where the difference to the
 // correctly rounded fp32 forms is below half an fp16 ulp except at rounding ties.
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
-__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// SwiGLU backward of two adjacent columns with autograd's fp16 rounding points:
+//   d = f16(dact), ds = f16(d * u), dup = f16(d * f16(g * sig)),
+//   dgate = f16(f32(ds) * sig * (1 + g * (1 - sig))), sig = 1 / (1 + e^-g) in fp32.
+// A product of two fp16 values is exact in fp32, so rounding it once to fp16 is the fp16
+// multiply (__hmul2_rn); the fp32 chain of dgate uses paired, non-contracted operations.
+// g2 / u2 / dg2 / du2 hold fp16 pairs (column c in the low half, c + 1 in the high half).
+__device__ __forceinline__ void swiglu_bwd_pair(float d0, float d1, uint32_t g2, uint32_t u2, uint32_t& dg2,
+                                                uint32_t& du2) {
+  const __half2 dh = __floats2half2_rn(d0, d1);
+  const __half2 gh = *reinterpret_cast<const __half2*>(&g2);
+  const __half2 uh = *reinterpret_cast<const __half2*>(&u2);
+  const float2 one = make_float2(1.0f, 1.0f);
+  const float2 g = __half22float2(gh);
+  const float2 t = __fmul2_rn(g, make_float2(-kLog2e, -kLog2e));
+  const float2 y = __fadd2_rn(make_float2(ex2_approx(t.x), ex2_approx(t.y)), one);
+  const float2 sig = make_float2(rcp_approx(y.x), rcp_approx(y.y));
+  const __half2 du = __hmul2_rn(dh, __float22half2_rn(__fmul2_rn(g, sig)));
+  const float2 ds = __half22float2(__hmul2_rn(dh, uh));
+  const float2 om = __ffma2_rn(sig, make_float2(-1.0f, -1.0f), one);  // 1 - sig, rounded once
+  const float2 q = __fadd2_rn(one, __fmul2_rn(g, om));
+  const __half2 dg = __float22half2_rn(__fmul2_rn(__fmul2_rn(ds, sig), q));
+  dg2 = *reinterpret_cast<const uint32_t*>(&dg);
+  du2 = *reinterpret_cast<const uint32_t*>(&du);
+}
+
+// Word i (fp16 pair i) of 32 consecutive fp16 values held as four 16-byte vectors.
+__device__ __forceinline__ uint32_t pair_word(const uint4 (&q)[4], int i) {
+  const uint4& v = q[i >> 2];
+  return (i & 3) == 0 ? v.x : (i & 3) == 1 ? v.y : (i & 3) == 2 ? v.z : v.w;
+}
 
 // TMA store of one staged [32 rows x 64 cols] fp16 sub-tile (128B-swizzled).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
@@ -511,70 +546,27 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
       st.flush(om.c2, col, yrow);
     }
   } else if constexpr (EPI == kSwigluB) {
+    // The 1-SM kernel's form (the 2-SM kernel pipelines its own, swiglu_bwd_epilogue2): the gate / up
+    // rows straight from global memory, 64-column outputs through the warp's staging buffer.
     const int F = p.swiglu_F;
 #pragma unroll 1
     for (int cp = 0; cp < 2; ++cp) {
       const int c0 = half * 4 + cp * 2;
       const int col0 = nb * BN + c0 * 32;
       if (col0 >= F) break;
-      // One 32-column part at a time (TMEM and the gate / up rows in, fp16 pairs out), so the
-      // live state stays small enough for the loads of a part to be in flight together.
-      uint4 ga[8], ua[8];  // this row's 64 gate / up values, from the TMA boxes when staged
-      if (aux) {
-        // The caller requested this tile's first box; this warp requests the second as soon as
-        // the first is in registers, so its load overlaps the arithmetic below.
-        if (!warp_wait_bar(aux->bar, aux->phase, aux->abort_flag, p, kStatusGemmEpilogueWait)) return;
-        aux->phase ^= 1u;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int off = lane * 128 + ((c ^ (lane & 7)) << 4);
-          ga[c] = *reinterpret_cast<const uint4*>(aux->buf + off);
-          ua[c] = *reinterpret_cast<const uint4*>(aux->buf + kAuxWarpBytes / 2 + off);
-        }
-        __syncwarp();
-        const int next_col = nb * BN + (half * 4 + 2) * 32;
-        if (cp == 0 && next_col < F && lane == 0) aux->issue(next_col, yrow);
-      }
       uint32_t pdg[2][16], pdu[2][16];
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
         uint32_t r[32];
         tmem_ld32(tl + c0 * 32 + part * 32, r);
         uint4 gq[4], uq[4];
-        if (aux) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            gq[j] = ga[part * 4 + j];
-            uq[j] = ua[part * 4 + j];
-          }
-        } else {
-          load_raw32(p.aux0, p.ld_aux, row, col0 + part * 32, p.M, F, gq);
-          load_raw32(p.aux1, p.ld_aux, row, col0 + part * 32, p.M, F, uq);
-        }
+        load_raw32(p.aux0, p.ld_aux, row, col0 + part * 32, p.M, F, gq);
+        load_raw32(p.aux1, p.ld_aux, row, col0 + part * 32, p.M, F, uq);
         tmem_ld_wait();
-        float d[32], g[32], u[32];
-        to_f32(r, d);
-        unpack32(gq, g);
-        unpack32(uq, u);
-        float sig[32], s16[32], ds[32];
-        round_all(d);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          sig[i] = sigmoid_f(g[i]);
-          s16[i] = g[i] * sig[i];
-          ds[i] = __fmul_rn(d[i], u[i]);
-        }
-        round_all(s16);
-        round_all(ds);
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float du0 = __fmul_rn(d[i], s16[i]), du1 = __fmul_rn(d[i + 1], s16[i + 1]);
-          const float dg0 = __fmul_rn(__fmul_rn(ds[i], sig[i]), 1.0f + __fmul_rn(g[i], 1.0f - sig[i]));
-          const float dg1 = __fmul_rn(__fmul_rn(ds[i + 1], sig[i + 1]), 1.0f + __fmul_rn(g[i + 1], 1.0f - sig[i + 1]));
-          __half2 hg = __floats2half2_rn(dg0, dg1), hu = __floats2half2_rn(du0, du1);
-          pdg[part][i / 2] = *reinterpret_cast<uint32_t*>(&hg);
-          pdu[part][i / 2] = *reinterpret_cast<uint32_t*>(&hu);
-        }
+        for (int i = 0; i < 16; ++i)
+          swiglu_bwd_pair(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]), pair_word(gq, i), pair_word(uq, i),
+                          pdg[part][i], pdu[part][i]);
       }
       st.begin();
       st.put_packed(0, pdg[0]);
@@ -586,6 +578,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om
       st.flush(om.c1, col0, yrow);
     }
   }
+  (void)aux;
 }
 
 template <int EPI, bool A_MN, bool B_MN>
@@ -830,6 +823,137 @@ __device__ __forceinline__ void tile_coords2(const Params& p, int t, int& mb2, i
   nb = r / rows;
 }
 
+// SwiGLU-backward epilogue of the 2-SM kernel. Each epilogue warp walks its parts (32 rows x 32
+// columns: tile columns nb*256 + half*128 + 32j, j < 4) in order across its tiles. A part's gate / up
+// boxes (32 x 32 fp16 each, 64B-swizzled, 4 KiB together) land in one of the warp's two slots,
+// requested two parts ahead and across tile boundaries, so the loads overlap the arithmetic of the
+// parts before; dgate and dup leave through the two halves of the warp's 4 KiB staging buffer by
+// two TMA stores, so a part waits only for the stores of the part before it. The accumulator is
+// released once its last part is in registers.
+constexpr uint32_t kSwbSlotBytes = 2 * 32 * 32 * 2;  // gate + up box of one part
+static_assert(2 * kSwbSlotBytes == kAuxWarpBytes && kSwbSlotBytes == kStageOutBytes, "per-warp buffer sizes");
+
+// This warp's first column and row in tile t, and how many of its four parts hold columns < F.
+__device__ __forceinline__ void swb_coords(const Params& p, int t, int half, int quarter, uint32_t rank, int& x0,
+                                           int& y, int& n) {
+  int mb2, nb, s;
+  tile_coords2(p, t, mb2, nb, s);
+  x0 = nb * BN + half * 128;
+  y = (mb2 * 2 + (int)rank) * BM + quarter * 32;
+  n = min(4, max(0, (p.swiglu_F - x0 + 31) / 32));
+}
+
+// The next part a warp requests: tile t (first column x0, first row y, n parts in the warp's columns),
+// part j; parts requested so far.
+struct SwbCursor {
+  int t, j, n, x0, y, requested;
+};
+
+__device__ __forceinline__ int swb_chunk(int lane, int c) {  // 64B swizzle: 16-byte chunk c of row `lane`
+  return lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4);
+}
+
+__device__ __forceinline__ void swiglu_bwd_epilogue2(const Params& p, const CUtensorMap* gate_map,
+                                                     const CUtensorMap* up_map, const CUtensorMap* dgate_map,
+                                                     const CUtensorMap* dup_map, uint8_t* slots, uint64_t* slot_bars,
+                                                     uint8_t* stage, uint32_t tmem_base, uint64_t* acc_full,
+                                                     uint32_t leader_acc_empty0, uint32_t leader_acc_empty1,
+                                                     volatile int* abort_flag, int cluster_id, int num_clusters,
+                                                     int num_tiles, int half, int quarter, uint32_t rank, int lane) {
+  SwbCursor rq{cluster_id, 0, 0, 0, 0, 0};
+  if (rq.t < num_tiles) swb_coords(p, rq.t, half, quarter, rank, rq.x0, rq.y, rq.n);
+  // Requests the next part's boxes into slot (requested & 1); the warp has finished reading that slot.
+  auto request = [&]() {
+    while (rq.j >= rq.n) {
+      if (rq.t >= num_tiles) return;
+      rq.t += num_clusters;
+      rq.j = 0;
+      if (rq.t >= num_tiles) return;
+      swb_coords(p, rq.t, half, quarter, rank, rq.x0, rq.y, rq.n);
+    }
+    if (lane == 0) {
+      const int sl = rq.requested & 1;
+      const int x = rq.x0 + rq.j * 32;
+      fence_proxy_async_smem();  // generic reads of the slot before the async-proxy refill
+      mbar_expect_tx(&slot_bars[sl], kSwbSlotBytes);
+      tma_load_2d(slots + sl * kSwbSlotBytes, gate_map, &slot_bars[sl], x, rq.y);
+      tma_load_2d(slots + sl * kSwbSlotBytes + kSwbSlotBytes / 2, up_map, &slot_bars[sl], x, rq.y);
+    }
+    ++rq.requested;
+    ++rq.j;
+  };
+  request();
+  request();
+  int consumed = 0, local = 0;
+  bool ok = true;
+  for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++local) {
+    const int acc = local & 1;
+    if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p, kStatusGemmEpilogueWait)) break;
+    tc_fence_after();
+    const uint32_t tl = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+    int x0, y, nparts;
+    swb_coords(p, t, half, quarter, rank, x0, y, nparts);
+    bool released = false;
+#pragma unroll 1
+    for (int j = 0; j < nparts; ++j) {
+      const int x = x0 + j * 32;
+      const bool last = j == nparts - 1;
+      uint32_t r[32];
+      tmem_ld32(tl + (half * 4 + j) * 32, r);
+      const int sl = consumed & 1;
+      if (!warp_wait_bar(&slot_bars[sl], (consumed >> 1) & 1, abort_flag, p, kStatusGemmEpilogueWait)) {
+        tmem_ld_wait();
+        ok = false;
+        break;
+      }
+      const uint8_t* src = slots + sl * kSwbSlotBytes;
+      tmem_ld_wait();
+      if (last) {  // the accumulator is in registers: the MMA may refill it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
+        released = true;
+      }
+      if (lane == 0) bulk_wait_read_all();  // the previous part's stores have left the staging buffer
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {  // one 16-byte chunk (8 columns) of gate / up in, dgate / dup out
+        const uint4 gq = *reinterpret_cast<const uint4*>(src + swb_chunk(lane, c));
+        const uint4 uq = *reinterpret_cast<const uint4*>(src + kSwbSlotBytes / 2 + swb_chunk(lane, c));
+        const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
+        uint32_t dg[4], du[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = 4 * c + i;
+          swiglu_bwd_pair(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]), gw[i], uw[i], dg[i], du[i]);
+        }
+        *reinterpret_cast<uint4*>(stage + swb_chunk(lane, c)) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+        *reinterpret_cast<uint4*>(stage + kSwbSlotBytes / 2 + swb_chunk(lane, c)) = make_uint4(du[0], du[1], du[2], du[3]);
+      }
+      // All lanes have read the slot and written the staging buffer: the slot is refilled (two parts
+      // ahead) and the results leave, both by the async proxy.
+      fence_proxy_async_smem();
+      __syncwarp();
+      request();
+      ++consumed;
+      if (lane == 0) {
+        tma_store_2d(dgate_map, stage, x, y);
+        tma_store_2d(dup_map, stage + kSwbSlotBytes / 2, x, y);
+        bulk_commit();
+      }
+    }
+    if (ok && !released) {  // no part of this tile in this warp's columns
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
+    }
+  }
+  // Requests still in flight (after an abandoned wait): let them land before the CTA leaves.
+  for (; consumed < rq.requested; ++consumed)
+    if (lane == 0) mbar_wait(&slot_bars[consumed & 1], (consumed >> 1) & 1, nullptr, 0);
+  __syncwarp();
+}
+
 template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -848,8 +972,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = bars + S2;
   uint64_t* acc_full = bars + 2 * S2;
   uint64_t* acc_empty = bars + 2 * S2 + 2;
-  uint64_t* aux_full = bars + 2 * S2 + 4;  // one per epilogue warp (kSwigluB, kRope)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S2 + 4 + kEpiWarps);
+  uint64_t* aux_full = bars + 2 * S2 + 4;  // two per epilogue warp (kSwigluB: one per slot; kRope: the first)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S2 + 4 + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -858,7 +982,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool leader = (rank == 0);
 
   if (threadIdx.x == 0) {
-    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&aux_full[w], 1);
+    for (int w = 0; w < 2 * kEpiWarps; ++w) mbar_init(&aux_full[w], 1);
     for (int s = 0; s < S2; ++s) {
       mbar_init(&full[s], 1);   // leader's producer arms it; both CTAs' TMA bytes complete it
       mbar_init(&empty[s], 1);  // the leader's MMA commit arrives in both CTAs
@@ -968,6 +1092,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) umma2_commit_both(&acc_full[acc]);
       }
     }
+  } else if constexpr (EPI == kSwigluB) {
+    const uint32_t leader_acc_empty0 = map_to_rank(smem_u32(&acc_empty[0]), 0);
+    const uint32_t leader_acc_empty1 = map_to_rank(smem_u32(&acc_empty[1]), 0);
+    swiglu_bwd_epilogue2(p, &tmX0, &tmX1, &tmC0, &tmC1, sAux + (warp - 2) * kAuxWarpBytes, &aux_full[2 * (warp - 2)],
+                         sOut + (warp - 2) * kStageOutBytes, tmem_base, acc_full, leader_acc_empty0, leader_acc_empty1,
+                         abort_flag, cluster_id, num_clusters, num_tiles, (warp - 2) >> 2, warp & 3, rank, lane);
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   } else {
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
@@ -981,11 +1113,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int mb2, nb, s;
       tile_coords2(p, t, mb2, nb, s);
       const int acc = local & 1;
-      if constexpr (EPI == kSwigluB) {
-        // This warp's first gate / up boxes of the tile load while the accumulator is awaited.
-        const int x = nb * BN + half * 4 * 32, y = (mb2 * 2 + (int)rank) * BM + quarter * 32;
-        if (x < p.swiglu_F && lane == 0) aux.issue(x, y);
-      } else if constexpr (EPI == kRope) {
+      if constexpr (EPI == kRope) {
         // The cos / sin rows of this warp's 32 token rows (consecutive positions).
         const int y = (mb2 * 2 + (int)rank) * BM + quarter * 32;
         if (p.rope_tma && nb * BN + half * 128 < p.rope_cols && lane == 0) aux.issue(0, y % p.rope_seq);
@@ -993,7 +1121,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
       epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb2 * 2 + (int)rank, nb, s,
-                         (EPI == kSwigluB || (EPI == kRope && p.rope_tma)) ? &aux : nullptr);
+                         (EPI == kRope && p.rope_tma) ? &aux : nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
@@ -1172,15 +1300,16 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
-                   uint32_t box_inner, uint32_t box_outer) {
+                   uint32_t box_inner, uint32_t box_outer, int swizzle_bytes) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {ld * 2};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -1236,18 +1365,23 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
          make_tmap_f16(&tc1, p.out1, p.swiglu_F, p.M, p.ld_out, 64, 32) &&
          make_tmap_f16(&tc2, p.out2, p.swiglu_F, p.M, p.ld_out, 64, 32);
   } else if constexpr (EPI == kSwigluB) {
-    ok = make_tmap_f16(&tc0, p.C, p.swiglu_F, p.M, p.ldc, 64, 32) &&
-         make_tmap_f16(&tc1, p.C + p.swiglu_F, p.swiglu_F, p.M, p.ldc, 64, 32);
+    // 2-SM kernel: 32 x 32 boxes (64B swizzle) per part; 1-SM kernel: 32 x 64 staging boxes.
+    const uint32_t bx = two_sm ? 32 : 64;
+    const int sw = two_sm ? 64 : 128;
+    ok = make_tmap_f16(&tc0, p.C, p.swiglu_F, p.M, p.ldc, bx, 32, sw) &&
+         make_tmap_f16(&tc1, p.C + p.swiglu_F, p.swiglu_F, p.M, p.ldc, bx, 32, sw);
   }
   if constexpr (EPI == kWgrad) {
     if (p.splits > 1) ok = make_tmap_f32(&tc0, p.ws, p.N, p.M, p.N, 32, 32);
   }
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for the output", name);
-  // The SwiGLU-backward epilogue's gate / up inputs, read as 32 x 64 boxes.
+  // The 2-SM SwiGLU-backward epilogue's gate / up inputs, read as 32 x 32 boxes (64B swizzle).
   CUtensorMap tx0 = tc0, tx1 = tc0;
-  if constexpr (EPI == kSwigluB)
-    ok = make_tmap_f16(&tx0, p.aux0, p.swiglu_F, p.M, p.ld_aux, 64, 32) &&
-         make_tmap_f16(&tx1, p.aux1, p.swiglu_F, p.M, p.ld_aux, 64, 32);
+  if constexpr (EPI == kSwigluB) {
+    if (two_sm)
+      ok = make_tmap_f16(&tx0, p.aux0, p.swiglu_F, p.M, p.ld_aux, 32, 32, 64) &&
+           make_tmap_f16(&tx1, p.aux1, p.swiglu_F, p.M, p.ld_aux, 32, 32, 64);
+  }
   // The RoPE epilogue's cos / sin tables ([rope_seq, 32] fp32): a warp's 32 rows are 32 consecutive
   // positions when rope_seq is a multiple of 32, one 32 x 32 box per table.
   if constexpr (EPI == kRope) {

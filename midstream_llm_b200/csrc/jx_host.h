@@ -58,11 +58,12 @@ enum DeviceStatus : int {
   kStatusCeBadTarget = 202,
 };
 
-// Builds a 2-D fp16 TMA descriptor with 128-byte swizzle.
+// Builds a 2-D fp16 TMA descriptor with 128-byte (or 64-byte) swizzle.
 //   inner: elements along the contiguous dimension, outer: rows,
-//   ld: elements between consecutive rows, box: {box_inner, box_outer}.
+//   ld: elements between consecutive rows, box: {box_inner, box_outer}
+//   (box_inner * 2 bytes <= swizzle_bytes).
 bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
-                   uint32_t box_inner, uint32_t box_outer);
+                   uint32_t box_inner, uint32_t box_outer, int swizzle_bytes = 128);
 
 // The same for fp32 tensors (box_inner * 4 bytes <= swizzle_bytes; 128- or 64-byte swizzle).
 bool make_tmap_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,

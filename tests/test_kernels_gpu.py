@@ -196,6 +196,42 @@ def test_swiglu_fwd_bwd(ops, gemm_mode):
     assert rel_err(dgu[:, F:], uf.grad) < TOL
 
 
+def _swiglu_bwd_recipe(dact, gate, up):
+    """The fp16-autocast rounding points of silu(gate) * up's backward, in fp32 torch ops:
+    d = f16(dact); dup = f16(d * f16(silu(g))); ds = f16(d * u); dgate = f16(ds * s * (1 + g * (1 - s)))."""
+    d = dact.half().float()
+    g, u = gate.float(), up.float()
+    s = torch.sigmoid(g)
+    dup = (d * (g * s).half().float()).half()
+    ds = (d * u).half().float()
+    dgate = (ds * s * (1.0 + g * (1.0 - s))).half()
+    return dgate, dup
+
+
+# (4000, 1024, 2816): the production shape with clipped rows and several tiles per CTA pair (the
+# 2-SM epilogue requests gate / up boxes across tile boundaries); (512, 256, 688): a partial last part.
+@pytest.mark.parametrize("M,d,F", [(4000, 1024, 2816), (512, 256, 688)])
+def test_swiglu_bwd_kernels_agree(ops, M, d, F):
+    from midstream_llm_b200 import _lib
+    gate, up = _h(M, F, seed=20), _h(M, F, seed=21)
+    # Small integers times multiples of 1/64: every partial sum is exact in fp32, so both kernels hold the
+    # same accumulators whatever their summation order, and their epilogues must agree bit for bit.
+    dy = _h(M, d, scale=1.0, seed=22).float().round().clamp(-2, 2).half()
+    wd = (_h(d, F, scale=0.3, seed=23).float() * 64).round().clamp(-64, 64).div(64).half()
+    outs = []
+    try:
+        for mode in (1, 2):
+            _lib.call("jx_gemm_set_mode", mode)
+            outs.append(ops.gemm_swiglu_bwd(dy, wd, gate, up))
+    finally:
+        _lib.call("jx_gemm_set_mode", 0)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])  # one formula, bit for bit, in both kernels' epilogues
+    dgate, dup = _swiglu_bwd_recipe(dy.float() @ wd.float(), gate, up)
+    assert rel_err(outs[1][:, :F], dgate.float()) < TOL
+    assert rel_err(outs[1][:, F:], dup.float()) < TOL
+
+
 # (2048, 2112, 704): the production q/k/v weight gradient, partial tiles in both output dimensions.
 @pytest.mark.parametrize("splits,T,N,K", [(1, 2048, 1024, 512), (4, 2048, 1024, 512), (3, 2048, 2112, 704)])
 def test_wgrad(ops, gemm_mode, splits, T, N, K):
