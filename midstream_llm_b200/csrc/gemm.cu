@@ -1541,6 +1541,7 @@ extern "C" int jx_gemm_swiglu_bwd(const void* dY, int64_t lddy, const void* Wd, 
   JX_CHECK_ARG(gate && up && dgu && aligned16(gate) && aligned16(up) && aligned16(dgu),
                "jx_gemm_swiglu_bwd: buffers must be 16-byte aligned");
   JX_CHECK_ARG(F % 8 == 0 && ld_gu % 8 == 0 && ld_dgu % 8 == 0, "jx_gemm_swiglu_bwd: F, ld_gu, ld_dgu must be multiples of 8");
+  JX_CHECK_ARG(ld_gu >= F && ld_dgu >= 2 * (int64_t)F, "jx_gemm_swiglu_bwd: rows shorter than F (gate / up) or 2F (dgu)");
   Params p = base_params(M, F, K);
   p.swiglu_F = F;
   p.C = static_cast<__half*>(dgu);

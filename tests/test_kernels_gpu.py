@@ -232,6 +232,20 @@ def test_swiglu_bwd_kernels_agree(ops, M, d, F):
     assert rel_err(outs[1][:, F:], dup.float()) < TOL
 
 
+def test_swiglu_bwd_repeatable(ops):
+    """The pipelined 2-SM epilogue (gate / up requested ahead across tiles, staging reused per part) gives the
+    same bits on every run: no part reads a slot or a staging buffer that another request is still filling."""
+    M, d, F = 16384, 1024, 2816
+    gate, up = _h(M, F, seed=30), _h(M, F, seed=31)
+    dy, wd = _h(M, d, seed=32), _h(d, F, scale=0.05, seed=33)
+    first = ops.gemm_swiglu_bwd(dy, wd, gate, up)
+    out = torch.empty_like(first)
+    for _ in range(4):
+        out.fill_(float("nan"))
+        ops.gemm_swiglu_bwd(dy, wd, gate, up, out=out)
+        assert torch.equal(out, first)
+
+
 # (2048, 2112, 704): the production q/k/v weight gradient, partial tiles in both output dimensions.
 @pytest.mark.parametrize("splits,T,N,K", [(1, 2048, 1024, 512), (4, 2048, 1024, 512), (3, 2048, 2112, 704)])
 def test_wgrad(ops, gemm_mode, splits, T, N, K):

