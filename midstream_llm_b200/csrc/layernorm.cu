@@ -17,11 +17,12 @@
 #include "jx_common.cuh"
 #include "jx_host.h"
 
+extern "C" int jx_rmsnorm_bwd_parts(int64_t rows);
+
 namespace jx {
 namespace ln {
 
 constexpr int kWarps = 8;
-constexpr int kMaxParts = 296;
 
 __device__ __forceinline__ float2 h2f2(uint32_t w) {
   return __half22float2(*reinterpret_cast<const __half2*>(&w));
@@ -257,8 +258,7 @@ extern "C" int jx_layernorm_bwd(const void* dy, const void* x, const float* mean
                "jx_layernorm_bwd: cols must be a multiple of 8 in (0, 4096]");
   JX_CHECK_ARG(aligned16(dy) && aligned16(x) && aligned16(dx) && aligned16(gamma) && (!dresid || aligned16(dresid)),
                "jx_layernorm_bwd: buffers must be 16-byte aligned");
-  int64_t parts = (rows + kWarps - 1) / kWarps;
-  const int grid = (int)(parts < kMaxParts ? parts : kMaxParts);
+  const int grid = jx_rmsnorm_bwd_parts(rows);  // the partial count the caller allocated
   const size_t smem = (size_t)kWarps * cols * sizeof(float);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const __half* dyh = static_cast<const __half*>(dy);
