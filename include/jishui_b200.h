@@ -71,7 +71,8 @@ int jx_rmsnorm_fwd(const void* x, const void* resid, void* sum_out, const float*
                    int64_t rows, int cols, float eps, jx_stream_t stream);
 /* Backward: dx = f16( dresid + f16(d rmsnorm/dx . dy) ) (dresid optional).
  * dy is f16 [rows, cols]; x is the forward input s; dgamma_part is f32
- * [nparts, cols] with nparts = jx_rmsnorm_bwd_parts(rows); reduce it with
+ * [nparts, cols] with nparts = jx_rmsnorm_bwd_parts(rows) (one per SM of the
+ * current device, at most 296, fewer for short inputs); reduce it with
  * jx_rmsnorm_dgamma_reduce. */
 int jx_rmsnorm_bwd_parts(int64_t rows);
 int jx_rmsnorm_bwd(const void* dy, const void* x, const float* rstd, const float* gamma, const void* dresid,

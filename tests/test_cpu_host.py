@@ -29,7 +29,9 @@ def test_library_exports_every_declared_symbol():
 
 def test_pure_host_queries():
     from midstream_llm_b200 import _lib
-    assert _lib.query("jx_rmsnorm_bwd_parts", 16384) == 296
+    # one norm-backward block (one partial row) per SM, 148 without a device; fewer for short inputs
+    assert _lib.query("jx_rmsnorm_bwd_parts", 16384) == 148
+    assert _lib.query("jx_rmsnorm_bwd_parts", 100) == 13
     assert _lib.query("jx_grad_stats_parts", 238_322_688) >= 148
     assert _lib.query("jx_gemm_wgrad_workspace_bytes", 1024, 1024, 4) == 1024 * 1024 * 4
     assert _lib.query("jx_gemm_wgrad_workspace_bytes", 1024, 1024, 1) == 0
