@@ -20,6 +20,7 @@ namespace rms {
 
 constexpr int kWarps = 8;
 constexpr int kMaxParts = 296;
+constexpr int kFwdBlocksPerSm = 2;  // forward grid: blocks of kWarps warps resident per SM (96 registers)
 
 __device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
   const uint4 u = *reinterpret_cast<const uint4*>(p);
@@ -44,6 +45,9 @@ __device__ __forceinline__ void store8(__half* p, const float (&v)[8]) {
 
 __device__ __forceinline__ float r16(float x) { return __half2float(__float2half_rn(x)); }
 
+// Grid-stride over rows (a grid of a few resident blocks per SM): each warp loads its next row
+// (and residual row) into registers before it finishes the current one, so a load round trip
+// overlaps every row's arithmetic and stores instead of being waited out per row.
 template <int NV>
 __global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_kernel(const __half* __restrict__ x,
                                                                   const __half* __restrict__ resid,
@@ -52,41 +56,71 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_kernel(const __half* 
                                                                   __half* __restrict__ y, float* __restrict__ rstd,
                                                                   int64_t rows, int cols, float eps) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5);
+  const int64_t step = (int64_t)gridDim.x * kWarps;
+  int64_t row = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const __half* xr = x + row * cols;
-  float v[NV][8];
-  float ss = 0.f;
+  uint4 xq[NV], rq[NV];
+  auto load_row = [&](int64_t r) {
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = (i * 32 + lane) * 8;
-    if (c < cols) {
-      load8(xr + c, v[i]);
-      if (resid) {
-        float r[8];
-        load8(resid + row * cols + c, r);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = r16(v[i][j] + r[j]);
-        store8(sum_out + row * cols + c, v[i]);
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < cols) {
+        xq[i] = *reinterpret_cast<const uint4*>(x + r * cols + c);
+        if (resid) rq[i] = *reinterpret_cast<const uint4*>(resid + r * cols + c);
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
     }
-  }
-  ss = warp_sum(ss);
-  const float rs = 1.0f / sqrtf(ss / (float)cols + eps);
-  if (lane == 0) rstd[row] = rs;
+  };
+  load_row(row);
+  for (; row < rows; row += step) {
+    float v[NV][8];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = (i * 32 + lane) * 8;
-    if (c < cols) {
-      float o[8];
-      const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
-      const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
-      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < cols) {
+        const __half2* h = reinterpret_cast<const __half2*>(&xq[i]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = r16(v[i][j] * rs) * g[j];
-      store8(y + row * cols + c, o);
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h[j]);
+          v[i][2 * j] = f.x;
+          v[i][2 * j + 1] = f.y;
+        }
+        if (resid) {
+          const __half2* rh = reinterpret_cast<const __half2*>(&rq[i]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(rh[j]);
+            v[i][2 * j] = r16(v[i][2 * j] + f.x);
+            v[i][2 * j + 1] = r16(v[i][2 * j + 1] + f.y);
+          }
+        }
+      }
+    }
+    if (row + step < rows) load_row(row + step);  // the next row is in flight during this one
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < cols) {
+        if (resid) store8(sum_out + row * cols + c, v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+      }
+    }
+    ss = warp_sum(ss);
+    const float rs = 1.0f / sqrtf(ss / (float)cols + eps);
+    if (lane == 0) rstd[row] = rs;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < cols) {
+        float o[8];
+        const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+        const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = r16(v[i][j] * rs) * g[j];
+        store8(y + row * cols + c, o);
+      }
     }
   }
 }
@@ -453,7 +487,9 @@ extern "C" int jx_rmsnorm_fwd(const void* x, const void* resid, void* sum_out, c
   JX_CHECK_ARG(aligned16(x) && aligned16(y) && aligned16(gamma) && (!resid || (aligned16(resid) && aligned16(sum_out))),
                "jx_rmsnorm_fwd: buffers must be 16-byte aligned");
   const int nv = pick_nv(cols);
-  const unsigned grid = (unsigned)((rows + kWarps - 1) / kWarps);
+  const int64_t blocks = (rows + kWarps - 1) / kWarps;
+  const int64_t resident = (int64_t)num_sms() * kFwdBlocksPerSm;
+  const unsigned grid = (unsigned)(blocks < resident ? blocks : resident);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const __half* xh = static_cast<const __half*>(x);
   const __half* rh = static_cast<const __half*>(resid);
