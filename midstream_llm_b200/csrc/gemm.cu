@@ -871,10 +871,9 @@ __device__ __forceinline__ void swiglu_bwd_epilogue2(const Params& p, const CUte
       if (rq.t >= num_tiles) return;
       swb_coords(p, rq.t, half, quarter, rank, rq.x0, rq.y, rq.n);
     }
-    if (lane == 0) {
+    if (lane == 0) {  // the caller has fenced the warp's generic reads of the slot against this refill
       const int sl = rq.requested & 1;
       const int x = rq.x0 + rq.j * 32;
-      fence_proxy_async_smem();  // generic reads of the slot before the async-proxy refill
       mbar_expect_tx(&slot_bars[sl], kSwbSlotBytes);
       tma_load_2d(slots + sl * kSwbSlotBytes, gate_map, &slot_bars[sl], x, rq.y);
       tma_load_2d(slots + sl * kSwbSlotBytes + kSwbSlotBytes / 2, up_map, &slot_bars[sl], x, rq.y);
