@@ -164,8 +164,10 @@ class GradReducer:
         all-reduce's traffic. GradScaler.unscale_ folds the 1/world_size of the
         mean into its unscale pass over the local shard and all-reduces only
         its partial sums of squares and the inf flag; AdamW updates the local
-        shard and all-gathers the fp16 weights in place. Each rank's fp32 master
-        weights and moments are current on its own shard only:
+        shard and all-gathers the fp16 weights in place, and the fp32 values the
+        kernels read (norm gains and biases) are shared by `sync_f32_params`.
+        Otherwise each rank's fp32 master weights and moments are current on its
+        own shard only:
         `gather_full_state(optimizer)` (a collective: every rank calls it)
         makes them whole again, e.g. before rank 0 writes a checkpoint.
     """
@@ -225,6 +227,19 @@ class GradReducer:
         """All ranks' updated fp16 shards into every rank's fp16 weight copy (in place)."""
         lo, hi = self.shard_range(flat)
         dist.all_gather_into_tensor(flat.p16, flat.p16[lo:hi], group=self.group)
+
+    def sync_f32_params(self, flat) -> None:
+        """After a sharded update: the parameters the kernels read in fp32 (norm gains and biases,
+        `flat.f32_read_index`) get their owner's new value on every rank. Each rank contributes the
+        elements of its own shard and zeros elsewhere; the sum is exact (one non-zero per element)."""
+        idx = getattr(flat, "f32_read_index", None)
+        if idx is None or idx.numel() == 0:
+            return
+        lo, hi = self.shard_range(flat)
+        vals = flat.p32.index_select(0, idx)
+        vals = torch.where((idx >= lo) & (idx < hi), vals, torch.zeros_like(vals))
+        dist.all_reduce(vals, op=dist.ReduceOp.SUM, group=self.group)
+        flat.p32.index_copy_(0, idx, vals)
 
     def gather_full_state(self, optimizer=None) -> None:
         """Makes the fp32 master weights (and the optimizer's moments) whole on every rank. A collective."""

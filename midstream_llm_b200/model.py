@@ -176,6 +176,10 @@ class FlatParams:
                 view = self.p32_view(n, p.shape)
                 view.copy_(p.detach().to(device=device, dtype=torch.float32))
                 p.data = view
+        # Flat indices of the parameters the kernels read in fp32 (the 1-D norm gains and biases; every matrix
+        # is read from the fp16 copy). A sharded update must hand their new values to every rank.
+        idx = [torch.arange(self.offsets[n], self.offsets[n] + p.numel()) for n, p in named if p.dim() == 1]
+        self.f32_read_index = (torch.cat(idx) if idx else torch.zeros(0, dtype=torch.long)).to(device)
         self._versions: list[int] | None = None
         self.generation = 0  # bumped whenever the fp16 weights are rewritten (caches derived from them go stale)
         # Per-update state filled by GradScaler.unscale_ / clip_grad_norm_ and

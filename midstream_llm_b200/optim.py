@@ -126,8 +126,9 @@ class AdamW(torch.optim.Optimizer):
         ops.adamw_step(flat.p32[lo:hi], flat.g32[lo:hi], self._m[lo:hi], self._v[lo:hi], flat.p16[lo:hi],
                        flat.inv_scale, flat.clip, flat.found_inf, self._step_state, group["lr"], beta1, beta2,
                        group["eps"], group["weight_decay"])
-        if red is not None:  # every rank's updated fp16 shard to every rank
+        if red is not None:  # every rank's updated fp16 shard, and the fp32 norm parameters, to every rank
             red.gather_f16(flat)
+            red.sync_f32_params(flat)
         flat.mark_f16_current()
         flat.inv_scale = flat.clip = flat.found_inf = None
         flat.stats_ready = False

@@ -81,6 +81,17 @@ def main():
     rs = train_update(ms, opt_s, sc_s, lambda: [(x3, y3)], 1, 1.0, 1e-3)
     rr = train_update(mr, opt_r, sc_r, lambda: [(x3, y3)], 1, 1.0, 1e-3)
     fs, fr = ms.flat(), mr.flat()
+    # The norm gains are read by the kernels in fp32: after the sharded update every rank holds the
+    # owner's new values (no gather_full_state needed), equal to the replicated update's.
+    norm32 = fs.p32.index_select(0, fs.f32_read_index)
+    n32 = [torch.empty_like(norm32) for _ in range(world)]
+    dist.all_gather(n32, norm32)
+    norm_equal_ranks = all(torch.equal(g, n32[0]) for g in n32)
+    norm_err = float((norm32 - fr.p32.index_select(0, fr.f32_read_index)).norm() / norm32.norm())
+    # A second update from the updated weights: the sharded and replicated losses still agree.
+    x4, y4 = batch(rank + 90, dev)
+    rs2 = train_update(ms, opt_s, sc_s, lambda: [(x4, y4)], 1, 1.0, 1e-3)
+    rr2 = train_update(mr, opt_r, sc_r, lambda: [(x4, y4)], 1, 1.0, 1e-3)
     lo, hi = ms.grad_reducer.shard_range(fs)
     shard_grad_err = float((fs.g32[lo:hi] - fr.g32[lo:hi]).norm() / fr.g32[lo:hi].norm())
     g16 = [torch.empty_like(fs.p16) for _ in range(world)]
@@ -92,7 +103,8 @@ def main():
     m_err = float((opt_s._m - opt_r._m).norm() / opt_r._m.norm())
     sharded = {"shard_grad_err": shard_grad_err, "f16_equal_ranks": f16_equal_ranks, "f16_err": f16_err,
                "p32_err": p32_err, "m_err": m_err, "grad_norm": [rs["grad_norm"], rr["grad_norm"]],
-               "loss": [rs["loss"], rr["loss"]]}
+               "loss": [rs["loss"], rr["loss"]], "norm_equal_ranks": norm_equal_ranks, "norm_err": norm_err,
+               "loss2": [rs2["loss"], rr2["loss"]]}
     if rank == 0:
         ref = model_on(dev)
         for rr in range(world):

@@ -139,6 +139,58 @@ def test_sharded_reducer_gloo_two_ranks():
     assert shards == {(0, 8224), (8224, 16448)}
 
 
+class _FakeFlatP:
+    def __init__(self, n, rank, idx):
+        g = torch.Generator().manual_seed(200 + rank)
+        self.p32 = torch.randn(n, generator=g)
+        self.numel = n
+        self.f32_read_index = idx
+
+
+def _sync_worker(rank, world, port, out_q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from midstream_llm_b200.distributed import GradReducer
+        n = 16448
+        # three fp32-read ranges: inside shard 0, straddling the boundary at 8224, inside shard 1
+        idx = torch.cat([torch.arange(100, 356), torch.arange(8000, 8512), torch.arange(12000, 12100)])
+        flat = _FakeFlatP(n, rank, idx)
+        before = flat.p32.clone()
+        owners = [_FakeFlatP(n, r, idx).p32 for r in range(world)]
+        red = GradReducer(shard_optimizer=True)
+        red.sync_f32_params(flat)
+        size = red.shard_size(n)
+        want = torch.stack([owners[int(i) // size][int(i)] for i in idx])
+        ok_idx = torch.equal(flat.p32[idx], want)
+        mask = torch.ones(n, dtype=torch.bool)
+        mask[idx] = False
+        ok_rest = torch.equal(flat.p32[mask], before[mask])
+        dist.barrier()
+        dist.destroy_process_group()
+        out_q.put((rank, ok_idx, ok_rest))
+    except Exception:
+        out_q.put((rank, "error", traceback.format_exc()))
+
+
+def test_sharded_update_shares_fp32_norm_parameters_gloo():
+    """After a sharded update each rank holds new master weights on its own shard only; the parameters the
+    kernels read in fp32 (norm gains and biases) must then carry their owner's value on every rank, including
+    a range that straddles the shard boundary, while everything else stays as it was."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sync_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for r in results:
+        assert r[1] != "error", r[2]
+        assert r[1] and r[2], r
+
+
 def _dead_rank_worker(rank, world, port, out_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime

@@ -46,3 +46,6 @@ def test_dp_matches_single_process_accumulation(tmp_path):
     assert sh["f16_equal_ranks"], sh
     assert sh["f16_err"] < 1e-3 and sh["p32_err"] < 1e-6 and sh["m_err"] < 1e-5, sh
     assert abs(sh["grad_norm"][0] - sh["grad_norm"][1]) <= 1e-5 * sh["grad_norm"][1], sh
+    # norm gains (read in fp32 by the kernels) carry the owner's update on every rank
+    assert sh["norm_equal_ranks"] and sh["norm_err"] < 1e-6, sh
+    assert abs(sh["loss2"][0] - sh["loss2"][1]) <= 2e-5 * abs(sh["loss2"][1]), sh
