@@ -71,7 +71,6 @@ class KVCacheDecoder:
         # step reuses them while the model still holds the same storage object.
         fl = self._fl if self._fl is not None and self.model._flat is self._fl else self.model.flat()
         fl.refresh_f16()
-        fl.wait_f16()  # a sharded update's fp16 shards may still be arriving
         n = len(self.context)
         if 0 < n < len(ctx) and ctx[:n] == self.context and fl.generation == self._generation and fl is self._fl:
             for p in range(n, len(ctx)):
@@ -79,7 +78,6 @@ class KVCacheDecoder:
         else:
             fl = self.model.flat()
             fl.refresh_f16()
-            fl.wait_f16()
             self._fl = fl
             self._prefill(ctx)
         self.context = ctx

@@ -164,9 +164,8 @@ class GradReducer:
         all-reduce's traffic. GradScaler.unscale_ folds the 1/world_size of the
         mean into its unscale pass over the local shard and all-reduces only
         its partial sums of squares and the inf flag; AdamW updates the local
-        shard, the fp32 values the kernels read (norm gains and biases) are
-        shared by `sync_f32_params`, and each rank's fp16 shard is broadcast to
-        the others, overlapping the next forward (`broadcast_f16`).
+        shard and all-gathers the fp16 weights in place, and the fp32 values the
+        kernels read (norm gains and biases) are shared by `sync_f32_params`.
         Otherwise each rank's fp32 master weights and moments are current on its
         own shard only:
         `gather_full_state(optimizer)` (a collective: every rank calls it)
@@ -224,19 +223,10 @@ class GradReducer:
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
         dist.all_reduce(found_inf, op=dist.ReduceOp.SUM, group=self.group)
 
-    def broadcast_f16(self, flat) -> None:
-        """All ranks' updated fp16 shards into every rank's fp16 weight copy, one broadcast per owner in rank
-        (= flat) order, left in flight: `flat.p16_pending` lists them and the next forward waits for a shard
-        only before it first reads weights in it (`FlatParams.wait_f16`), so the later shards arrive while
-        the first layers run. Every rank issues the same broadcasts in the same order."""
-        size = self.shard_size(flat.numel)
-        pending = []
-        for r in range(self.world_size()):
-            src = r if self.group is None else dist.get_global_rank(self.group, r)
-            work = dist.broadcast(flat.p16[r * size:(r + 1) * size], src=src, group=self.group, async_op=True)
-            pending.append((r * size, (r + 1) * size, work))
-            self.collectives += 1
-        flat.p16_pending = pending
+    def gather_f16(self, flat) -> None:
+        """All ranks' updated fp16 shards into every rank's fp16 weight copy (in place)."""
+        lo, hi = self.shard_range(flat)
+        dist.all_gather_into_tensor(flat.p16, flat.p16[lo:hi], group=self.group)
 
     def sync_f32_params(self, flat) -> None:
         """After a sharded update: the parameters the kernels read in fp32 (norm gains and biases,

@@ -180,8 +180,6 @@ class FlatParams:
         # is read from the fp16 copy). A sharded update must hand their new values to every rank.
         idx = [torch.arange(self.offsets[n], self.offsets[n] + p.numel()) for n, p in named if p.dim() == 1]
         self.f32_read_index = (torch.cat(idx) if idx else torch.zeros(0, dtype=torch.long)).to(device)
-        # fp16 ranges still arriving from their owner rank after a sharded update: (lo, hi, collective).
-        self.p16_pending: list = []
         self._versions: list[int] | None = None
         self.generation = 0  # bumped whenever the fp16 weights are rewritten (caches derived from them go stale)
         # Per-update state filled by GradScaler.unscale_ / clip_grad_norm_ and
@@ -220,22 +218,10 @@ class FlatParams:
                 return False
         return True
 
-    def wait_f16(self, upto: int | None = None) -> None:
-        """Orders the current stream after the arrival of every pending fp16 range (from a sharded update's
-        broadcasts) that starts below flat index `upto`; all of them when `upto` is None."""
-        keep = []
-        for lo, hi, work in self.p16_pending:
-            if upto is None or lo < upto:
-                work.wait()
-            else:
-                keep.append((lo, hi, work))
-        self.p16_pending = keep
-
     def refresh_f16(self, force: bool = False) -> None:
         """Re-casts the fp16 weight copy if any parameter was modified in place."""
         versions = [p._version for p in self.params]
         if force or versions != self._versions:
-            self.wait_f16()
             ops.cast_f32_f16(self.p32, self.p16)
             self._versions = versions
             self.generation += 1
@@ -401,18 +387,6 @@ class JishuiForCausalLM(nn.Module):
         return ws
 
     # ---- weight views ------------------------------------------------------
-    def _layer_ends(self, fl: FlatParams) -> list[int]:
-        """Flat index just past each layer's parameters."""
-        ends = getattr(self, "_ends_cache", None)
-        if ends is None or ends[0] is not fl:
-            out = []
-            for i in range(self.config.num_hidden_layers):
-                pre = f"layers.{i}."
-                out.append(max(fl.offsets[n] + p.numel() for n, p in zip(fl.names, fl.params) if n.startswith(pre)))
-            ends = (fl, out)
-            self._ends_cache = ends
-        return ends[1]
-
     def _layer_weights(self, fl: FlatParams, i: int):
         c = self.config
         d, F = c.hidden_size, c.intermediate_size
@@ -479,13 +453,10 @@ class JishuiForCausalLM(nn.Module):
         fl = self.flat()
         fl.refresh_f16()
         ws = self._workspace(B, T, train)
-        ends = self._layer_ends(fl)
-        fl.wait_f16(fl.offsets["embed_tokens.weight"] + c.vocab_size * c.hidden_size)
         e16 = fl.p16_rows("embed_tokens.weight", c.vocab_size, c.hidden_size)
         ops.embed_fwd(ids.reshape(-1), e16, out=ws.xs[0])
         ckpt = train and c.gradient_checkpointing
         for i in range(c.num_hidden_layers):
-            fl.wait_f16(ends[i])  # a sharded update's later shards keep arriving while these layers run
             w = self._layer_weights(fl, i)
             if train:
                 x_in, x_out = ws.xs[i], ws.xs[i + 1]

@@ -122,17 +122,13 @@ class AdamW(torch.optim.Optimizer):
             flat.prepare_grads()  # zero-fill parameters that received no gradient
         beta1, beta2 = group["betas"]
         red = _shard_reducer(flat)
-        flat.wait_f16()  # the last update's fp16 broadcasts (if any) are done before this one rewrites p16
         lo, hi = (0, flat.numel) if red is None else red.shard_range(flat)
         ops.adamw_step(flat.p32[lo:hi], flat.g32[lo:hi], self._m[lo:hi], self._v[lo:hi], flat.p16[lo:hi],
                        flat.inv_scale, flat.clip, flat.found_inf, self._step_state, group["lr"], beta1, beta2,
                        group["eps"], group["weight_decay"])
-        if red is not None:
-            # The fp32 norm parameters to every rank (a small all-reduce the compute stream waits for), then
-            # every rank's fp16 shard, left in flight for the next forward to wait on shard by shard; the
-            # communication stream runs them in this order.
+        if red is not None:  # every rank's updated fp16 shard, and the fp32 norm parameters, to every rank
+            red.gather_f16(flat)
             red.sync_f32_params(flat)
-            red.broadcast_f16(flat)
         flat.mark_f16_current()
         flat.inv_scale = flat.clip = flat.found_inf = None
         flat.stats_ready = False

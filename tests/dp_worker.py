@@ -81,8 +81,6 @@ def main():
     rs = train_update(ms, opt_s, sc_s, lambda: [(x3, y3)], 1, 1.0, 1e-3)
     rr = train_update(mr, opt_r, sc_r, lambda: [(x3, y3)], 1, 1.0, 1e-3)
     fs, fr = ms.flat(), mr.flat()
-    assert fs.p16_pending, "the sharded update leaves its fp16 broadcasts in flight"
-    fs.wait_f16()
     # The norm gains are read by the kernels in fp32: after the sharded update every rank holds the
     # owner's new values (no gather_full_state needed), equal to the replicated update's.
     norm32 = fs.p32.index_select(0, fs.f32_read_index)
@@ -94,7 +92,6 @@ def main():
     x4, y4 = batch(rank + 90, dev)
     rs2 = train_update(ms, opt_s, sc_s, lambda: [(x4, y4)], 1, 1.0, 1e-3)
     rr2 = train_update(mr, opt_r, sc_r, lambda: [(x4, y4)], 1, 1.0, 1e-3)
-    fs.wait_f16()
     lo, hi = ms.grad_reducer.shard_range(fs)
     shard_grad_err = float((fs.g32[lo:hi] - fr.g32[lo:hi]).norm() / fr.g32[lo:hi].norm())
     g16 = [torch.empty_like(fs.p16) for _ in range(world)]

@@ -191,57 +191,6 @@ def test_sharded_update_shares_fp32_norm_parameters_gloo():
         assert r[1] and r[2], r
 
 
-class _FakeFlatH:
-    def __init__(self, n, rank):
-        self.p16 = torch.full((n,), float(rank + 1), dtype=torch.float16)
-        self.numel = n
-        self.p16_pending = []
-
-
-def _broadcast_worker(rank, world, port, out_q):
-    try:
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-        dist.init_process_group("gloo", rank=rank, world_size=world)
-        from midstream_llm_b200.distributed import GradReducer
-        from midstream_llm_b200.model import FlatParams
-        n = 16448
-        flat = _FakeFlatH(n, rank)
-        red = GradReducer(shard_optimizer=True)
-        red.broadcast_f16(flat)
-        size = red.shard_size(n)
-        pending = [(lo, hi) for lo, hi, _ in flat.p16_pending]
-        FlatParams.wait_f16(flat, upto=size)  # only the first shard's broadcast is awaited
-        left = [(lo, hi) for lo, hi, _ in flat.p16_pending]
-        FlatParams.wait_f16(flat)
-        want = torch.cat([torch.full((size,), float(r + 1), dtype=torch.float16) for r in range(world)])
-        ok = torch.equal(flat.p16, want) and not flat.p16_pending
-        dist.barrier()
-        dist.destroy_process_group()
-        out_q.put((rank, ok, pending, left))
-    except Exception:
-        out_q.put((rank, "error", traceback.format_exc()))
-
-
-def test_sharded_fp16_broadcasts_gloo():
-    """After a sharded update every rank's fp16 shard goes to every rank, one broadcast per owner in flat order;
-    the broadcasts stay pending until a reader waits, and waiting up to a flat index waits only for the
-    shards that start below it."""
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_broadcast_worker, args=(r, 2, port, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    results = [q.get(timeout=120) for _ in procs]
-    for p in procs:
-        p.join(timeout=60)
-    for r in results:
-        assert r[1] != "error", r[2]
-        rank, ok, pending, left = r
-        assert ok, r
-        assert pending == [(0, 8224), (8224, 16448)] and left == [(8224, 16448)], r
-
-
 def _dead_rank_worker(rank, world, port, out_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
