@@ -106,7 +106,8 @@ def _optimizers(ref, mine):
 
 
 def test_tiny_config_ten_updates_losses_and_gradients():
-    """BASELINE's tiny debug config: 10 updates, each update's loss and every parameter's gradient."""
+    """The tiny debug decoder (V 24000, d 256, 4 layers, seq 256, batch 4): 10 updates, each update's loss and
+    every parameter's gradient."""
     from midstream_llm_b200.model import causal_lm_loss
     cfg = _tiny()
     ref, mine = _pair(cfg, 0)
@@ -123,7 +124,8 @@ def test_tiny_config_ten_updates_losses_and_gradients():
 
 @pytest.mark.slow
 def test_200m_micro_batch_loss_and_gradients():
-    """The 200M architecture at micro-batch 16 x 1024 (BASELINE's step): loss and every parameter gradient."""
+    """The 200M architecture at micro-batch 16 x 1024 (the single-GPU training step): loss and every parameter
+    gradient."""
     from midstream_llm_b200.model import causal_lm_loss
     cfg = _200m()
     ref, mine = _pair(cfg, 0)
