@@ -1,7 +1,7 @@
 """Generates the golden fixtures that pin the oracle to the reference.
 
 Run where the reference project is available; MIDSTREAM_REF must name its
-`src` directory (the one holding the `jishui` package). The GPU box never runs this.
+`src` directory (the one holding the `jishui` package). The tests only read the fixtures it writes.
 
     MIDSTREAM_REF=<reference checkout>/src python tests/golden/make_golden.py
 
