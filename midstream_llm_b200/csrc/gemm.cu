@@ -192,9 +192,9 @@ __device__ __forceinline__ void to_f32(const uint32_t (&r)[32], float (&v)[32]) 
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// silu(x) = x / (1 + e^-x), sigmoid(x) = 1 / (1 + e^-x) with the fast exp and
-// division; the results are rounded to fp16, where the difference to the
-// correctly rounded fp32 forms is below half an fp16 ulp except at rounding ties.
+// silu(x) = x / (1 + e^-x) with the fast exp and division; the result is rounded
+// to fp16, where the difference to the correctly rounded fp32 form is below half an
+// fp16 ulp except at rounding ties. (The backward's sigmoid: swiglu_bwd_pair.)
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
