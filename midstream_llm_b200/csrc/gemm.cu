@@ -52,10 +52,6 @@ enum Epi : int { kF16 = 0, kRope = 1, kSwigluF = 2, kSwigluB = 3, kWgrad = 4, kH
 struct Params {
   int M, N, K;
   int tiles_m, tiles_n, splits, kb_per_split, num_kb;
-  // 2-SM kernel work units: units < full_units are whole 256 x 256 tiles (in tile order); the rest are the
-  // remaining tiles cut into two 256 x 128 halves each (plain / residual epilogue only), so a last wave that
-  // would leave most CTA pairs idle runs as one wave of half tiles.
-  int full_units, units;
   int swiglu_F;  // kSwigluF: row offset of the up half inside B; kSwigluB: F
   // outputs
   __half* C;
@@ -343,20 +339,16 @@ struct OutMaps {
 // weight-gradient output with direct 16-byte accesses.
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile(const Params& p, const OutMaps& om, Stager& st, uint32_t tacc,
-                                              int quarter, int half, int lane, int mb, int nb, int split, AuxTma* aux = nullptr,
-                                              int narrow_sub = -1) {
+                                              int quarter, int half, int lane, int mb, int nb, int split, AuxTma* aux = nullptr) {
   const int row = mb * BM + quarter * 32 + lane;
   const int yrow = mb * BM + quarter * 32;  // first row of this warp's TMA boxes
   const uint32_t tl = tacc + (static_cast<uint32_t>(quarter * 32) << 16);
   if constexpr (EPI == kF16 || EPI == kHeadCE || EPI == kWgrad) {
     float ce_m = -INFINITY, ce_s = 0.f;  // kHeadCE: running statistics of this thread's 128-column block
-    // A half tile (narrow_sub >= 0, plain / residual epilogue only): 128 accumulator columns, this warp's 64
-    // of them at tile columns narrow_sub * 128 + half * 64.
-    const int ncp = narrow_sub >= 0 ? 1 : 2;
 #pragma unroll 1
-    for (int cp = 0; cp < ncp; ++cp) {
-      const int c0 = narrow_sub >= 0 ? half * 2 : half * 4 + cp * 2;  // first of two 32-column TMEM chunks
-      const int col0 = narrow_sub >= 0 ? nb * BN + narrow_sub * 128 + half * 64 : nb * BN + c0 * 32;
+    for (int cp = 0; cp < 2; ++cp) {
+      const int c0 = half * 4 + cp * 2;  // first of two 32-column chunks
+      const int col0 = nb * BN + c0 * 32;
       if (col0 >= p.N) break;
       uint32_t r0[32], r1[32];
       tmem_ld32(tl + c0 * 32, r0);
@@ -961,20 +953,6 @@ __device__ __forceinline__ void swiglu_bwd_epilogue2(const Params& p, const CUte
   __syncwarp();
 }
 
-// Work unit u of the 2-SM kernel: its tile (mb2, nb, split s) and, for a half tile, which 128-column half
-// (sub); returns whether u is a half tile.
-__device__ __forceinline__ bool unit_coords2(const Params& p, int u, int& mb2, int& nb, int& s, int& sub) {
-  if (u < p.full_units) {
-    tile_coords2(p, u, mb2, nb, s);
-    sub = 0;
-    return false;
-  }
-  const int v = u - p.full_units;
-  tile_coords2(p, p.full_units + (v >> 1), mb2, nb, s);
-  sub = v & 1;
-  return true;
-}
-
 template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -1031,8 +1009,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int tiles_m2 = (p.tiles_m + 1) / 2;
-  const int num_tiles = p.units;
-  (void)tiles_m2;
+  const int num_tiles = tiles_m2 * p.tiles_n * p.splits;
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
 
@@ -1041,8 +1018,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
-        int mb2, nb, s, sub;
-        const bool narrow = unit_coords2(p, t, mb2, nb, s, sub);
+        int mb2, nb, s;
+        tile_coords2(p, t, mb2, nb, s);
         const int m0 = mb2 * 256 + rank * 128;  // this CTA's A rows
         const int kb0 = s * p.kb_per_split;
         const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
@@ -1053,7 +1030,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t leader_full = map_to_rank(smem_u32(&full[stage]), 0);
-          if (leader) mbar_expect_tx(&full[stage], narrow ? 2 * (kAHalf + kBHalf / 2) : 2 * kStage2Bytes);
+          if (leader) mbar_expect_tx(&full[stage], 2 * kStage2Bytes);
           const uint32_t a_dst = smem_u32(smA + stage * kAHalf);
           const uint32_t b_dst = smem_u32(smB + stage * kBHalf);
           if constexpr (!A_MN) {
@@ -1062,13 +1039,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d_pair(a_dst, &tmA, leader_full, m0, kb * BK);
             tma_load_2d_pair(a_dst + 8192, &tmA, leader_full, m0 + 64, kb * BK);
           }
-          if (narrow) {  // half tile: this CTA's 64 of its 128 B rows (N 128 split over the pair)
-            const int n0 = nb * BN + sub * 128 + rank * 64;
-            if constexpr (!B_MN)
-              tma_load_2d_pair(b_dst, &tmX0, leader_full, kb * BK, n0);  // the 64-row B map
-            else
-              tma_load_2d_pair(b_dst, &tmB, leader_full, n0, kb * BK);
-          } else if constexpr (!B_MN) {
+          if constexpr (!B_MN) {
             int brow;
             if constexpr (EPI == kSwigluF)
               brow = (rank == 0 ? 0 : p.swiglu_F) + nb * 128;  // CTA 0: gate rows, CTA 1: up rows
@@ -1085,14 +1056,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc_wide = idesc_f16_f32(256, BN, A_MN, B_MN);
-      constexpr uint32_t idesc_narrow = idesc_f16_f32(256, BN / 2, A_MN, B_MN);
+      constexpr uint32_t idesc = idesc_f16_f32(256, BN, A_MN, B_MN);
       uint32_t it = 0;
       int local = 0;
       bool ok = true;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++local) {
-        int mb2, nb, s, sub;
-        const uint32_t idesc = unit_coords2(p, t, mb2, nb, s, sub) ? idesc_narrow : idesc_wide;
+        int mb2, nb, s;
+        tile_coords2(p, t, mb2, nb, s);
         const int kb0 = s * p.kb_per_split;
         const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         const int acc = local & 1;
@@ -1139,8 +1109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     AuxTma aux{sAux + (warp - 2) * kAuxWarpBytes, &aux_full[warp - 2], 0u, &tmX0, &tmX1, abort_flag};
     int local = 0;
     for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
-      int mb2, nb, s, sub;
-      const bool narrow = unit_coords2(p, t, mb2, nb, s, sub);
+      int mb2, nb, s;
+      tile_coords2(p, t, mb2, nb, s);
       const int acc = local & 1;
       if constexpr (EPI == kRope) {
         // The cos / sin rows of this warp's 32 token rows (consecutive positions).
@@ -1150,7 +1120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!warp_wait_bar(&acc_full[acc], (local >> 1) & 1, abort_flag, p, kStatusGemmEpilogueWait)) break;
       tc_fence_after();
       epilogue_tile<EPI>(p, om, st, tmem_base + acc * BN, quarter, half, lane, mb2 * 2 + (int)rank, nb, s,
-                         (EPI == kRope && p.rope_tma) ? &aux : nullptr, narrow ? sub : -1);
+                         (EPI == kRope && p.rope_tma) ? &aux : nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
@@ -1420,10 +1390,6 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
            make_tmap_f32(&tx1, p.rope_sin, 32, p.rope_seq, 32, 32, 32);
   }
   JX_CHECK_ARG(ok, "%s: cannot encode TMA descriptor for an epilogue input", name);
-  // The plain / residual epilogue's half tiles read 64 rows of a K-major B per CTA.
-  if constexpr (EPI == kF16 && !B_MN) {
-    JX_CHECK_ARG(make_tmap_f16(&tx0, B, p.K, b_rows, ldb, BK, 64), "%s: cannot encode TMA descriptor for B", name);
-  }
 
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (EPI == kSwigluF) ? (p.swiglu_F + 127) / 128 : (p.N + BN - 1) / BN;
@@ -1464,16 +1430,6 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Params
     if (max_cl > persistent_sms() / 2) max_cl = persistent_sms() / 2;
     const int tiles2 = ((p.tiles_m + 1) / 2) * p.tiles_n * p.splits;
     const int clusters = tiles2 < max_cl ? tiles2 : max_cl;
-    p.full_units = p.units = tiles2;
-    if constexpr (EPI == kF16) {
-      // A last wave of `rem` whole tiles on `clusters` pairs takes a whole tile's time while most pairs idle;
-      // as 2*rem half tiles (one wave when 2*rem <= clusters) it takes about 0.6 of it.
-      const int rem = tiles2 % clusters;
-      if (p.splits == 1 && tiles2 > clusters && rem > 0 && 2 * rem <= clusters) {
-        p.full_units = tiles2 - rem;
-        p.units = tiles2 + rem;
-      }
-    }
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     JX_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm2_kernel<EPI, A_MN, B_MN>, ta, tb, tc0, tc1, tc2, tx0, tx1, p), name);
     JX_CHECK_LAUNCH(name);

@@ -68,27 +68,6 @@ def test_gemm_resid_ragged(ops, gemm_mode, M, N, K):
     assert rel_err(ops.gemm_f16(a, b, resid=r2, out=r2), ref) < TOL
 
 
-# 16384 rows x 1024 (or a ragged 1000) output columns: 256 pair tiles on 74 CTA pairs leave a last wave of 34
-# tiles, which the 2-SM kernel runs as 68 half tiles (256 x 128). B K-major (a projection) and MN-major (an
-# input gradient), with and without the residual.
-@pytest.mark.parametrize("N", [1024, 1000])
-@pytest.mark.parametrize("b_mn", [False, True])
-@pytest.mark.parametrize("with_resid", [False, True])
-def test_gemm_last_wave_half_tiles(ops, N, b_mn, with_resid):
-    M, K = 16384, 512
-    a, b = _h(M, K, seed=60), _h(N, K, seed=61)
-    r = _h(M, N, seed=62) if with_resid else None
-    prod = a.float() @ b.float().t()
-    ref = r.float() + prod.half().float() if with_resid else prod
-    B = b.t().contiguous() if b_mn else b
-    c = ops.gemm_f16(a, B, b_mn_major=b_mn, resid=r)
-    torch.cuda.synchronize()
-    assert rel_err(c, ref) < TOL, rel_err(c, ref)
-    # every output tile written, the half tiles' columns included (no stale or unwritten block)
-    blk = (c.float() - ref.float()).abs().reshape(M // 256, 256, -1).amax(dim=(1, 2))
-    assert float(blk.max()) < 0.05 * float(ref.abs().max()), float(blk.max())
-
-
 @pytest.mark.parametrize("M", [1, 3, 8])
 def test_small_m_products(ops, M):
     """M <= 8 (incremental decoding) takes the weight-streaming path: plain, residual, q/k/v + RoPE at
