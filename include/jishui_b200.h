@@ -54,9 +54,10 @@ const char* jx_last_error(void);
 int64_t jx_launch_count(void);
 /* Device-side status word: non-zero when a kernel abandoned work after a
  * bounded wait expired (code identifies the wait: 101-103 GEMM producer / MMA /
- * epilogue, 301-303 attention producer / MMA / softmax, 401 the staged RMSNorm
- * backward's row copies) or met a bad input (201 token id, 202 target). Reads
- * and optionally clears it; synchronises the current device. */
+ * epilogue, 301-303 attention producer / MMA / softmax, 501 the staged RMSNorm
+ * backward's row copies) or met a bad input (201 token id, 202 target, 401 / 402
+ * packed-row column / source). Reads and optionally clears it; synchronises the
+ * current device. */
 int jx_device_status(int* status_out, int clear);
 /* Number of SMs that the persistent kernels (GEMM, attention) launched from the
  * calling host thread leave free, e.g. for NCCL's collective kernels while

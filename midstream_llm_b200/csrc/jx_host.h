@@ -56,7 +56,7 @@ enum DeviceStatus : int {
   kStatusGemmEpilogueWait = 103,
   kStatusEmbedBadId = 201,
   kStatusCeBadTarget = 202,
-  kStatusNormWait = 401,  // the staged RMSNorm backward's row-copy wait
+  kStatusNormWait = 501,  // the staged RMSNorm backward's row-copy wait
 };
 
 // Builds a 2-D fp16 TMA descriptor with 128-byte (or 64-byte) swizzle.
