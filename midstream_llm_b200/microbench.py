@@ -17,13 +17,17 @@ Shapes (the operator workload of the Jishui-200M step):
   eval     validation forward (no autograd, fused head + CE) of the 200M model at 16 x 1024
   decode   next-token logits with the KV cache vs re-running the whole context (200M, context ~1000)
 Each line is JSON with the time per call (CUDA events, after warm-up, inputs
-larger than L2 unless noted) and the achieved rate against the measured peaks.
+larger than L2 unless noted), the achieved rate against the measured peaks and
+the SM clock read just before the timed calls (`sm_mhz`). The B200 is power-capped:
+after seconds of dense GEMMs the SM clock drops (to ~1240 MHz) and takes a second
+or two to recover, so `--op all` pauses between operator groups.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import math
+import time
 from pathlib import Path
 
 import torch
@@ -41,10 +45,31 @@ def _peaks() -> dict:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "fallback": True}
 
 
+_NVML = None
+
+
+def _sm_mhz() -> int | None:
+    """Current SM clock of device 0 (NVML), or None where NVML is unavailable."""
+    global _NVML
+    try:
+        import pynvml
+        if _NVML is None:
+            pynvml.nvmlInit()
+            _NVML = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+        return int(pynvml.nvmlDeviceGetClockInfo(_NVML, pynvml.NVML_CLOCK_SM))
+    except Exception:
+        return None
+
+
+_LAST_MHZ = None
+
+
 def _time(fn, iters: int, warmup: int = 3) -> float:
+    global _LAST_MHZ
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    _LAST_MHZ = _sm_mhz()
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
     s.record()
@@ -57,7 +82,8 @@ def _time(fn, iters: int, warmup: int = 3) -> float:
 
 def _emit(name: str, seconds: float, work: float, unit: str, peak: float, **extra) -> dict:
     rate = work / seconds / (1e9 if unit == "GB/s" else 1e12)
-    line = {"op": name, "us": seconds * 1e6, "achieved": rate, "unit": unit, "peak": peak, "frac": rate / peak}
+    line = {"op": name, "us": seconds * 1e6, "achieved": rate, "unit": unit, "peak": peak, "frac": rate / peak,
+            "sm_mhz": _LAST_MHZ}
     line.update(extra)
     print(json.dumps(line), flush=True)
     return line
@@ -346,6 +372,9 @@ def main() -> None:
                      ("attn", bench_attn), ("eval", bench_eval),
                      ("decode", bench_decode)):
         if a.op in ("all", name):
+            if a.op == "all":
+                torch.cuda.synchronize()
+                time.sleep(3.0)  # let the SM clock recover from the previous group under the power cap
             fn(a.iters)
             torch.cuda.empty_cache()
 
